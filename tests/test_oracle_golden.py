@@ -1,0 +1,119 @@
+"""Pin the CPU oracle against fixtures produced by the reference's own code.
+
+Fixtures come from tests/golden/make_golden.py, which ran the reference's
+interop/pt_model.py MLPBlock/RMSNorm, interop/convert_checkpoint.py and
+bonsai-test/bitlinear.py.  These tests run on CPU only.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import GOLDEN
+
+
+def _load(name):
+    return np.load(os.path.join(GOLDEN, f"{name}.npz"))
+
+
+@pytest.mark.parametrize("case", ["swiglu_small", "swiglu_dead"])
+def test_swiglu_matches_reference_mlpblock(case):
+    z = _load(case)
+    out = O.swiglu_ffn(z["x"], (z["vg"], z["cg"], O.LAYOUT_IN_OUT), (z["vu"], z["cu"], O.LAYOUT_IN_OUT),
+                       (z["vd"], z["cd"], O.LAYOUT_IN_OUT))
+    assert O.rel_l2(out, z["out"]) < 1e-12
+
+
+def test_swiglu_residual_epilogue():
+    z = _load("swiglu_small")
+    out = O.swiglu_ffn(z["x"], (z["vg"], z["cg"], 0), (z["vu"], z["cu"], 0), (z["vd"], z["cd"], 0),
+                       add_residual=True)
+    assert O.rel_l2(out, z["out"] + z["x"]) < 1e-12
+
+
+def test_tile_layout_is_in_out():
+    """values[r, k] is [B_in, B_out] (convert_checkpoint.py:118-131)."""
+    z = _load("tile_layout")
+    v, c = O.dense_to_block_ell(z["W"], 64, 1.0)
+    np.testing.assert_array_equal(c, z["cols"])
+    np.testing.assert_array_equal(v, z["values"])
+    back = O.block_ell_to_dense(z["values"], z["cols"], 128, 256)
+    np.testing.assert_array_equal(back, z["back"])
+    x = np.random.default_rng(0).standard_normal((5, 256)).astype(np.float32)
+    y = O.block_ell_matmul(x, z["values"], z["cols"])
+    np.testing.assert_allclose(y, x.astype(np.float64) @ z["W"].T.astype(np.float64), rtol=1e-10, atol=1e-10)
+
+
+def test_out_in_layout_equivalent():
+    z = _load("tile_layout")
+    x = np.random.default_rng(1).standard_normal((7, 256))
+    y0 = O.block_ell_matmul(x, z["values"], z["cols"], O.LAYOUT_IN_OUT)
+    y1 = O.block_ell_matmul(x, np.swapaxes(z["values"], -1, -2), z["cols"], O.LAYOUT_OUT_IN)
+    np.testing.assert_allclose(y0, y1, rtol=0, atol=0)
+
+
+def test_rmsnorm_matches_reference():
+    z = _load("rmsnorm")
+    out = O.rmsnorm(z["x"], z["gain"], float(z["eps"]))
+    np.testing.assert_allclose(out, z["out"], rtol=1e-13, atol=1e-13)
+
+
+def test_loop_matches_reference_order():
+    z = _load("loop")
+    out = O.looped_ffn(z["h0"], z["gain"], (z["vg"], z["cg"], 0), (z["vu"], z["cu"], 0),
+                       (z["vd"], z["cd"], 0), L=int(z["L"]), eps=float(z["eps"]))
+    assert O.rel_l2(out, z["out"]) < 1e-12
+
+
+def test_ternary_quantizers_match_bitlinear():
+    z = _load("ternary")
+    t, s = O.ternary_quantize_tiles(z["vg"])
+    np.testing.assert_allclose(s.ravel(), z["s"], rtol=2e-7, atol=0)
+    np.testing.assert_array_equal(t, z["t"])
+    q, scale = O.activation_quantize_int(z["x"])
+    # the reference returns the dequantised activation q / scale
+    np.testing.assert_array_equal((q.astype(np.float32) / scale[:, None]).astype(np.float32), z["x_dq"])
+
+
+def test_ternary_matmul_matches_fake_quant_linear():
+    z = _load("ternary")
+    t, s = O.ternary_quantize_tiles(z["vg"])
+    q, scale = O.activation_quantize_int(z["x"])
+    y = O.ternary_block_ell_matmul(q, scale, t, s, z["cg"])
+    assert O.rel_l2(y, z["y"]) < 1e-6
+
+
+def test_pack_roundtrip_and_codes():
+    rng = np.random.default_rng(2)
+    t = rng.integers(-1, 2, size=(3, 2, 64, 64)).astype(np.int8)
+    p = O.pack_ternary(t)
+    assert p.shape == (3, 2, 64, 16) and p.dtype == np.uint8
+    np.testing.assert_array_equal(O.unpack_ternary(p), t)
+    # element (i=B_in 0, j=B_out 0) -> word 0 bits 0-1
+    t2 = np.zeros((1, 1, 64, 64), np.int8)
+    t2[0, 0, 1, 0] = -1  # B_in 1 of output column 0 -> bits 2-3 of word 0
+    w = O.pack_ternary(t2).view(np.uint32)
+    assert w[0, 0, 0, 0] == 0b1100
+
+
+def test_ternary_tile_sums_exact_int():
+    rng = np.random.default_rng(4)
+    T, B, R, K, C = 9, 64, 2, 2, 3
+    q = rng.integers(-128, 128, size=(T, C * B)).astype(np.int8)
+    t = rng.integers(-1, 2, size=(R, K, B, B)).astype(np.int8)
+    cols = np.array([[0, 2], [1, -1]], np.int32)
+    s_w = np.ones((R, K), np.float32)
+    y, sums = O.ternary_block_ell_matmul(q, np.ones(T, np.float32), t, s_w, cols, return_tile_sums=True)
+    ref = q[:, 0:64].astype(np.int64) @ t[0, 0].astype(np.int64)
+    np.testing.assert_array_equal(sums[(0, 0)], ref)
+    assert (1, 1) not in sums
+
+
+def test_random_topology_unique_sorted():
+    rng = np.random.default_rng(0)
+    c = O.random_topology(16, 32, 8, rng)
+    assert c.shape == (16, 8) and c.dtype == np.int32
+    for row in c:
+        assert len(np.unique(row)) == 8 and np.all(np.diff(row) > 0)
