@@ -1,0 +1,315 @@
+"""Benchmark: Block-ELL SwiGLU forward on B200 (BASELINE config 5 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 5]
+
+One step = one bf16 Block-ELL SwiGLU forward (gate/up + SiLU*up + down +
+residual) over the config's T tokens, inputs resident in HBM (x alone is
+2 GiB for config 5, larger than the 126 MB L2, so no flush is needed).  N>1
+splits the d_ff block-rows across ranks with one NCCL reduce-scatter of the
+down-projection partials (strong scaling: the job size is fixed).
+Rank 0 prints one JSON line.  ``--impl reference`` times the CPU restatement
+of the reference path (oracle/) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(ROOT, "looped-blockell-tpu_b200")
+for _p in (ROOT, PKG_ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "Block-ELL SwiGLU tokens/s & effective TFLOP/s per B200 (1/2/4/8 GPU) vs roofline"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline_sample(cfg, tokens: int, reps: int = 1):
+    """Time the oracle (numpy restatement of the reference gather+GEMM path)
+    on `tokens` tokens of `cfg` using every host core; returns tokens/s."""
+    import numpy as np
+    import oracle as O
+    from looped_blockell.synth import make_ffn
+    c = make_ffn(cfg, device="cpu", T=tokens)
+    f = {k: (v.float().numpy() if not k.startswith("c") else v.numpy()) for k, v in c.items()}
+    O.swiglu_ffn(f["x"][:8], (f["vg"], f["cg"], 0), (f["vu"], f["cu"], 0), (f["vd"], f["cd"], 0),
+                 dtype=np.float32)  # warm BLAS
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.swiglu_ffn(f["x"], (f["vg"], f["cg"], 0), (f["vu"], f["cu"], 0), (f["vd"], f["cd"], 0),
+                     add_residual=True, dtype=np.float32)
+    dt = time.perf_counter() - t0
+    return tokens * reps / dt, dt
+
+
+def run_reference(args, cfg, rank, world):
+    """CPU arm: the oracle port of the reference path on all host threads."""
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    cores = os.cpu_count()
+    sample = args.ref_tokens
+    vals = []
+    cpu_baseline_sample(cfg, sample // 4)  # warm-up (untimed)
+    for _ in range(max(args.warmup, 0)):
+        pass
+    for _ in range(args.steps):
+        v, _ = cpu_baseline_sample(cfg, sample)
+        vals.append(v)
+    value = statistics.median(vals)
+    ms = cfg.T / value * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg.name, "T": cfg.T, "d_model": cfg.d_model, "d_ff": cfg.d_ff, "B": cfg.B,
+                   "density": cfg.density, "sample_tokens": sample},
+        "tflops_effective": cfg.nnz_flops() / (ms / 1e3) / 1e12,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens of {cfg.name} per step, numpy gather+BLAS restatement of "
+                                   f"block_ell_matmul (oracle/bell_oracle.py), scaled linearly to T={cfg.T}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=5)
+    ap.add_argument("--shared-gate-up", action="store_true")
+    ap.add_argument("--ref-tokens", type=int, default=2048)
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    from looped_blockell.synth import CONFIGS
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, world)
+        return
+    run_gpu(args, cfg, rank, world)
+
+
+def _events(torch):
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def run_gpu(args, cfg, rank, world):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from looped_blockell.kernels import ops
+    from looped_blockell.synth import make_ffn
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
+    c = make_ffn(cfg, device="cuda", shared_gate_up=args.shared_gate_up)
+    T, d, F = cfg.T, cfg.d_model, cfg.d_ff
+    launches_per_step = 3
+    if world > 1:
+        from looped_blockell.dist import ShardedSwiGLU
+        model = ShardedSwiGLU(c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], rank, world)
+        step_out = model.alloc_out(T, c["x"])
+        launches_per_step = model.launches_per_step(T)
+
+        def step(x):
+            return model.forward(x, out=step_out)
+    else:
+        out = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
+        h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
+
+        def step(x):
+            return ops._swiglu(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], True, ops.TILE_IN_OUT, False,
+                               out=out, h=h)[0]
+
+    x = c["x"]
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = _events(torch)
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step(x)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = T / (ms / 1e3)
+    tflops = cfg.nnz_flops() / (ms / 1e3) / 1e12
+
+    # dominant kernel: the fused gate/up kernel, timed alone with events
+    gu = None
+    if world == 1:
+        from looped_blockell.kernels import _lib
+        import ctypes as C
+        lib = _lib.load()
+        desc = _lib.BellFFNDesc()
+        plan = torch.empty(ops.plan_bytes(c["vg"].shape[0], c["vg"].shape[1], c["vu"].shape[1], c["vd"].shape[0],
+                                          c["vd"].shape[1]), dtype=torch.uint8, device="cuda")
+        desc.T, desc.d_model, desc.d_ff, desc.dtype, desc.add_residual = T, d, F, 0, 1
+        desc.x, desc.h, desc.out, desc.plan = x.data_ptr(), h.data_ptr(), out.data_ptr(), plan.data_ptr()
+        B = cfg.B
+        desc.gate = ops._ell(c["vg"], c["cg"], d // B, 0)
+        desc.up = ops._ell(c["vu"], c["cu"], d // B, 0)
+        desc.down = ops._ell(c["vd"], c["cd"], F // B, 0)
+        s = ops._stream()
+        for _ in range(2):
+            _lib.check(lib.bell_gate_up_bf16(C.byref(desc), s), "gate_up")
+        g0, g1 = _events(torch)
+        n_gu = max(3, min(args.steps, 10))
+        g0.record()
+        for _ in range(n_gu):
+            _lib.check(lib.bell_gate_up_bf16(C.byref(desc), s), "gate_up")
+        g1.record()
+        torch.cuda.synchronize()
+        gu_ms = g0.elapsed_time(g1) / n_gu
+        R_f = F // B
+        gu_flops = 2.0 * T * B * B * 2 * R_f * cfg.K_gu
+        gu = dict(ms=gu_ms, tflops=gu_flops / (gu_ms / 1e3) / 1e12)
+
+    # end to end through the public op with host buffers
+    e2e = None
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        oh = torch.empty((T if world == 1 else step_out.shape[0], d), dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(x)
+        for _ in range(2):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(step(xd), non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a0, a1 = _events(torch)
+        n_e2e = max(3, min(args.steps, 5))
+        a0.record()
+        for _ in range(n_e2e):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(step(xd), non_blocking=True)
+        a1.record()
+        torch.cuda.synchronize()
+        ems = a0.elapsed_time(a1) / n_e2e
+        if world > 1:
+            t = torch.tensor([ems], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": T / (ems / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": xh.numel() * 2,
+               "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": ems}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "T": T, "d_model": d, "d_ff": F, "B": cfg.B, "density": cfg.density,
+                       "gate_up_topology": "shared" if args.shared_gate_up else "independent",
+                       "parallelism": f"dff{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (x is 2 GiB)"},
+            "tflops_effective": tflops, "tflops_effective_per_gpu": tflops / world,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(), "e2e": e2e,
+        }
+        if gu:
+            line["roofline"] = {"bound": "tensor", "kernel": "bell_bf16_kernel<gate/up>", "achieved": gu["tflops"],
+                                "peak": tc_peak, "unit": "TFLOP/s", "frac": gu["tflops"] / tc_peak,
+                                "peak_source": f"{peak_src} bf16 burst", "traffic": None,
+                                "kernel_ms": gu["ms"], "whole_step_frac": tflops / world / tc_peak}
+        if world == 1:
+            v, dt = cpu_baseline_sample(cfg, args.cpu_tokens)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"{args.cpu_tokens} tokens of {cfg.name} ({dt:.1f} s), numpy "
+                                              "restatement of the reference path, scaled linearly"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,242 @@
+/*
+ * bell.h — C ABI of the B200 (sm_100a) Block-ELL SwiGLU library (libbell_b200.so).
+ *
+ * Plain C: device pointers, sizes and a stream handle (a cudaStream_t passed
+ * as void*).  No torch types.  Every entry point is stream-ordered on the
+ * caller's stream, never synchronises (except bell_read_status), and never
+ * allocates or frees device memory: the caller owns inputs, outputs and the
+ * workspace buffers named in the descriptors.
+ *
+ * Return value: 0 (BELL_OK) or a negative BELL_ERR_* code; the message of the
+ * last failure on the calling thread is available from bell_last_error().
+ * Device-side problems (a column index out of range, a wait that timed out)
+ * never trap: the kernels record a BELL_ERR_* bit in the status word
+ * (BellFFNDesc.status, or the library's own word when NULL) and skip the work;
+ * bell_read_status() returns and clears it.
+ *
+ * Block-ELL weight (looped_blockell/layers/block_ell.py:1-9,53-66 of the
+ * reference): values [R, K, B, B] dense tiles and col_indices [R, K] int32.
+ * The logical weight is [R*B, C*B]; y = x @ W^T.  Tile layout
+ * BELL_TILE_IN_OUT (default) stores values[r,k] as [B_in, B_out], the
+ * JAX/Flax convention (block_ell.py:96-99); BELL_TILE_OUT_IN stores
+ * [B_out, B_in], the reference CUDA kernels' convention
+ * (csrc/block_ell/swiglu_fwd.cu:273-284).  A column index of -1 marks a dead
+ * slot (looped_blockell/opt/column_reorder.py:131-136) that contributes
+ * nothing.  B is 64 or 128.
+ */
+#ifndef BELL_H_
+#define BELL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BELL_ABI_VERSION 1
+
+enum {
+  BELL_OK = 0,
+  BELL_ERR_DTYPE = -1,   /* unsupported dtype / kind */
+  BELL_ERR_SHAPE = -2,   /* inconsistent or unsupported shape */
+  BELL_ERR_ALIGN = -3,   /* pointer or stride not 16-byte aligned */
+  BELL_ERR_ARCH = -4,    /* device is not sm_100 */
+  BELL_ERR_LAUNCH = -5,  /* CUDA API / launch failure */
+  BELL_ERR_TIMEOUT = -6, /* a device-side bounded wait gave up */
+  BELL_ERR_COLIDX = -7,  /* column index outside [-1, C) */
+  BELL_ERR_ARG = -8      /* NULL pointer or bad argument */
+};
+
+/* device status-word bits (OR-ed by kernels) */
+enum {
+  BELL_STATUS_COLIDX = 1,
+  BELL_STATUS_TIMEOUT = 2,
+  BELL_STATUS_INTERNAL = 4
+};
+
+enum { BELL_TILE_IN_OUT = 0, BELL_TILE_OUT_IN = 1 };
+enum { BELL_DTYPE_BF16 = 0, BELL_DTYPE_F32 = 1 };
+
+/* One Block-ELL weight. */
+typedef struct BellEll {
+  const void* values;          /* [R, K, B, B] bf16 or f32 tiles            */
+  const int32_t* col_indices;  /* [R, K]                                    */
+  int32_t R, C, K, B;          /* block-rows, block-cols, slots/row, tile   */
+  int32_t layout;              /* BELL_TILE_IN_OUT / BELL_TILE_OUT_IN        */
+  int32_t reserved;
+} BellEll;
+
+/*
+ * SwiGLU feed-forward: out = W_down(silu(W_gate x) * W_up x) (+ residual).
+ * x, residual, out: [T, d_model]; h, gate_pre, up_out: [T, d_ff]; row-major,
+ * contiguous, element type = dtype (bf16 or f32).  `plan` is caller-owned
+ * workspace of bell_plan_bytes() bytes (16-byte aligned).
+ */
+typedef struct BellFFNDesc {
+  int64_t T;
+  int32_t d_model, d_ff;
+  int32_t dtype;               /* BELL_DTYPE_BF16 / BELL_DTYPE_F32           */
+  int32_t add_residual;        /* add `residual` (or x when NULL) to out    */
+  const void* x;
+  const void* residual;        /* NULL -> x                                  */
+  void* h;                     /* workspace/output: silu(gate) * up          */
+  void* gate_pre;              /* optional output: gate projection (or NULL) */
+  void* up_out;                /* optional output: up projection (or NULL)   */
+  void* out;
+  void* plan;                  /* workspace                                  */
+  BellEll gate, up, down;
+  int32_t* status;             /* optional device status word (or NULL)      */
+} BellFFNDesc;
+
+/* y = x @ W^T (+ residual): one Block-ELL linear. */
+typedef struct BellLinearDesc {
+  int64_t T;
+  int32_t dtype;               /* element type of x and the weight tiles     */
+  int32_t out_dtype;           /* element type of out (bf16 inputs: BF16/F32) */
+  int32_t add_residual;
+  int32_t reserved;
+  const void* x;               /* [T, C*B]                                   */
+  const void* residual;        /* [T, R*B], element type = dtype              */
+  void* out;                   /* [T, R*B]                                   */
+  void* plan;                  /* workspace, bell_plan_bytes(0,0,0,R,K)      */
+  BellEll w;
+  int32_t* status;
+} BellLinearDesc;
+
+/* Workspace bytes for the tile-schedule plan of one forward. */
+size_t bell_plan_bytes(int32_t R_gu, int32_t K_gate, int32_t K_up, int32_t R_down, int32_t K_down);
+
+/*
+ * Fused Block-ELL SwiGLU forward, bf16 in/out, fp32 accumulation in TMEM.
+ * Replaces titan::block_ell_swiglu_fwd / _with_intermediate
+ * (reference csrc/block_ell/block_ell_ops.cpp:51-76, swiglu_fwd.cu:565-733).
+ */
+int bell_swiglu_fwd_bf16(const BellFFNDesc* desc, void* stream);
+
+/* Gate/up half only: h = silu(x Wg) * (x Wu) (+ gate_pre/up_out).
+ * Replaces the reference's first launch, block_ell_gate_up_silu_kernel
+ * (swiglu_fwd.cu:140-402, launched at :652). */
+int bell_gate_up_bf16(const BellFFNDesc* desc, void* stream);
+
+/* One Block-ELL linear (the down projection with residual epilogue, or any
+ * block_ell_matmul).  Replaces block_ell_down_residual_kernel
+ * (swiglu_fwd.cu:413-559, launched at :690) and the JAX block_ell_matmul
+ * (looped_blockell/layers/block_ell.py:149-182). */
+int bell_linear_bf16(const BellLinearDesc* desc, void* stream);
+
+/* fp32 SwiGLU forward (all tensors f32; accuracy target rel-L2 <= 1e-5). */
+int bell_swiglu_fwd_f32(const BellFFNDesc* desc, void* stream);
+int bell_linear_f32(const BellLinearDesc* desc, void* stream);
+
+/* ---------------------------------------------------------------- ternary */
+
+/*
+ * Ternary Block-ELL weight: 2-bit packed tiles and one fp32 scale per tile.
+ * packed: [R, K, B, B/4] bytes; tile (r,k) stored output-column major
+ * ([B_out][B_in]); each little-endian uint32 holds 16 consecutive B_in
+ * entries of one output column, entry i at bits 2*(i%16); codes 00 = 0,
+ * 01 = +1, 11 = -1.  scales: [R, K] fp32 (per-tile AbsMean,
+ * bonsai-test/bitlinear.py:34-55 with group = one tile).
+ */
+typedef struct BellTernaryEll {
+  const uint8_t* packed;
+  const float* scales;
+  const int32_t* col_indices;
+  int32_t R, C, K, B;
+} BellTernaryEll;
+
+/*
+ * Ternary SwiGLU forward.  x: [T, d_model] bf16.  Activations are quantised
+ * per token to int8 by absmax (bitlinear.py:58-69, Qb = 128, clamp 127);
+ * tile products accumulate exactly in int32 (tcgen05 kind::i8), are scaled
+ * per tile in fp32 in ascending slot order, and divided by the token scale;
+ * h = silu(gate) * up in fp32 is re-quantised per token over all of d_ff for
+ * the down projection.  out: [T, d_model] fp32 (+ x when add_residual).
+ * Workspaces (caller-owned): q_x int8 [T, d_model], s_x f32 [T],
+ * h f32 [T, d_ff], q_h int8 [T, d_ff], s_h f32 [T], plan.
+ * gate_pre / up_out: optional fp32 [T, d_ff] outputs.
+ */
+typedef struct BellTernaryFFNDesc {
+  int64_t T;
+  int32_t d_model, d_ff;
+  int32_t add_residual;
+  int32_t reserved;
+  const void* x;               /* bf16 */
+  int8_t* q_x;
+  float* s_x;
+  float* h;
+  int8_t* q_h;
+  float* s_h;
+  float* gate_pre;             /* optional */
+  float* up_out;               /* optional */
+  float* out;
+  void* plan;
+  BellTernaryEll gate, up, down;
+  int32_t* status;
+} BellTernaryFFNDesc;
+
+int bell_swiglu_fwd_ternary(const BellTernaryFFNDesc* desc, void* stream);
+
+/* ------------------------------------------------------------------- loop */
+
+/*
+ * L shared-weight iterations of  h <- h + FFN(RMSNorm(h))  in one persistent
+ * kernel (bf16).  Replaces titan::persistent_mlp_step's per-block host loop
+ * (csrc/loop/persistent_core.cu:273-337, loop_ops.cpp:52-66) for the
+ * shared-weight case.  h_in, h_out: [T, d_model]; norm_gain: [d_model] bf16;
+ * workspaces: hn [T, d_model] bf16, h_mid [T, d_ff] bf16, plan, and
+ * `barrier` (>= 64 bytes, zero-filled by the library on each call).
+ */
+typedef struct BellLoopDesc {
+  int64_t T;
+  int32_t d_model, d_ff;
+  int32_t L;
+  float eps;
+  const void* h_in;
+  void* h_out;
+  const void* norm_gain;
+  void* hn;
+  void* h_mid;
+  void* plan;
+  void* barrier;
+  BellEll gate, up, down;
+  int32_t* status;
+} BellLoopDesc;
+
+int bell_loop_fwd_bf16(const BellLoopDesc* desc, void* stream);
+
+/* Diagonal SSM injection h = exp(-softplus(log_dt) exp(log_A)) h + softplus(log_dt) e
+ * (bf16 h/e, fp32 log_A/log_dt [d]); replaces diagonal_injection_cuda
+ * (csrc/loop/persistent_core.cu:53-83). */
+int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const void* e,
+                             const float* log_A, const float* log_dt, void* out, void* stream);
+
+/* RMSNorm (bf16 in/out, fp32 math); replaces rmsnorm_cuda
+ * (csrc/loop/persistent_core.cu:97-154,224-264). */
+int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gain, float eps,
+                      void* out, void* stream);
+
+/* ---------------------------------------------------------------- L2 pins */
+
+/* Persisting-L2 window over [base, base+bytes) on `stream`; replaces
+ * pin_weights_l2 / unpin_weights_l2 (csrc/loop/l2_policy.cu:48-155). */
+int bell_pin_l2(const void* base, size_t bytes, void* stream);
+int bell_unpin_l2(void* stream);
+
+/* ------------------------------------------------------------------- misc */
+
+int bell_abi_version(void);
+/* Copies the last error message of this thread into buf; returns its code. */
+int bell_last_error(char* buf, size_t len);
+/* Reads (and clears when `clear`) the library's status word on `stream`;
+ * this call synchronises the stream. */
+int bell_read_status(int32_t* value, int32_t clear, void* stream);
+/* Number of SMs of the current device and whether it is sm_100 (1/0). */
+int bell_device_info(int32_t* sm_count, int32_t* is_sm100);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BELL_H_ */

@@ -1,0 +1,564 @@
+// bell_bf16.cu — bf16 Block-ELL kernels for sm_100a.
+//
+//   * gate/up kernel: h = silu(x Wg) * (x Wu), the SiLU*up epilogue fused;
+//     replaces block_ell_gate_up_silu_kernel (reference
+//     csrc/block_ell/swiglu_fwd.cu:140-402).
+//   * linear kernel: out = a W (+ residual); the down projection with its
+//     residual epilogue, replacing block_ell_down_residual_kernel
+//     (swiglu_fwd.cu:413-559), and the generic block_ell_matmul
+//     (looped_blockell/layers/block_ell.py:149-182).
+//
+// One persistent CTA per SM walks work units (128-token tile m, output
+// block-row r).  Warp roles:
+//   warp 0     TMA producer: per plan step, the activation tile
+//              [128 tokens x 64 K] (128-B swizzle, K-major) named by the
+//              step's column block, and the weight tile(s) [64 K x B]
+//              (MN-major for [B_in,B_out] tiles, K-major for [B_out,B_in]).
+//   warp 1     TMEM owner + single-thread tcgen05.mma issuer (M=128, fp32
+//              accumulators; gate and up side by side so a shared column
+//              block issues one N=2B MMA).
+//   warps 2-5  epilogue: tcgen05.ld, SiLU*up or +residual, bf16 stores.
+// Accumulators are double-buffered in TMEM so the epilogue of unit i
+// overlaps the MMAs of unit i+1.  Every wait is bounded (bell_ptx.cuh).
+#include <string>
+
+#include "bell_host.h"
+#include "bell_ptx.cuh"
+
+namespace bell {
+
+static constexpr int kBM = 128;        // tokens per tile (MMA M)
+static constexpr int kBK = 64;         // K elements per pipeline stage (128 B of bf16)
+static constexpr int kThreads = 192;   // 6 warps
+static constexpr uint32_t kNone = 255;
+
+template <int B, bool GU>
+struct Cfg {
+  static constexpr int A_BYTES = kBM * kBK * 2;         // 16 KB
+  static constexpr int W_BYTES = kBK * B * 2;           // 8 / 16 KB
+  static constexpr int STAGE_BYTES = A_BYTES + W_BYTES * (GU ? 2 : 1);
+  static constexpr int NS = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
+  static constexpr int ACC_COLS = GU ? 2 * B : B;       // fp32 columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;        // double buffered
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
+};
+
+struct Bf16Params {
+  int64_t T;
+  int32_t n_mtiles;
+  int32_t R;         // output block-rows
+  int32_t K0, K1;    // slots per row of w0 / w1
+  int32_t S;         // plan entries per row
+  const uint32_t* plan;
+  const int32_t* counts;
+  void* out;         // GU: h [T, R*B] bf16; linear: out [T, R*B]
+  int64_t ld_out;    // elements
+  void* gate_pre;    // GU optional
+  void* up_out;      // GU optional
+  const void* residual;  // linear optional (bf16, same shape as out)
+  int32_t add_residual;
+  int32_t out_f32;   // linear: write fp32 instead of bf16
+  int32_t* status;
+  uint64_t timeout_ns;
+};
+
+// Load one [64 K x B] weight chunk of tile `tile` (global tile index r*K+k).
+template <int B, bool W_MN>
+__device__ __forceinline__ void load_w_chunk(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int tile, int kc,
+                                             uint64_t pol) {
+  if constexpr (W_MN) {
+    // [B_in, B_out] tile rows are K; two 64-wide boxes when B = 128.
+#pragma unroll
+    for (int nh = 0; nh < B / 64; ++nh)
+      tma_load_2d(dst + nh * 8192, map, bar, nh * 64, tile * B + kc * kBK, pol);
+  } else {
+    // [B_out, B_in] tile rows are N; one box of 64 K x B rows.
+    tma_load_2d(dst, map, bar, kc * kBK, tile * B, pol);
+  }
+}
+
+template <int B, bool W_MN>
+__device__ __forceinline__ uint64_t w_desc(uint32_t w_addr, int kk) {
+  if constexpr (W_MN) return sdesc_sw128(w_addr + kk * 2048, 8192, 1024);
+  else return sdesc_sw128(w_addr + kk * 32, 16, 1024);
+}
+
+template <int B, bool GU, bool W_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    bell_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w0,
+                     const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
+  using C = Cfg<B, GU>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE_BYTES);
+  uint64_t* empty = full + C::NS;
+  uint64_t* acc_full = empty + C::NS;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  Ctl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int n_units = p.n_mtiles * p.R;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_w0);
+      if (GU) prefetch_tmap(&tm_w1);
+      const uint64_t pol_a = policy_evict_normal();
+      const uint64_t pol_w = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool alive = true;
+      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+        const int m = u / p.R, r = u % p.R;
+        const int n = p.counts[r] & 0xFFFF;
+        const uint32_t* plan = p.plan + size_t(r) * p.S;
+        for (int s = 0; s < n && alive; ++s) {
+          const uint32_t e = plan[s];
+          const int c = int(e & 0xFFFFu);
+          const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+          const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
+          const uint32_t bytes = C::A_BYTES + (has0 ? C::W_BYTES : 0) + (has1 ? C::W_BYTES : 0);
+          for (int kc = 0; kc < B / kBK; ++kc) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
+              alive = false;
+              break;
+            }
+            uint8_t* st = smem + stage * C::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[stage], bytes);
+            tma_load_2d(st, &tm_a, &full[stage], c * B + kc * kBK, m * kBM, pol_a);
+            if (has0) load_w_chunk<B, W_MN>(st + C::A_BYTES, &tm_w0, &full[stage], r * p.K0 + int(k0), kc, pol_w);
+            if (has1)
+              load_w_chunk<B, W_MN>(st + C::A_BYTES + C::W_BYTES, &tm_w1, &full[stage], r * p.K1 + int(k1), kc,
+                                    pol_w);
+            ++issued;
+            if (++stage == C::NS) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      if (!alive) {
+        // let the copies already issued land before the CTA exits
+        int st = stage, ph = phase;
+        for (int i = 0; i < C::NS && i < issued; ++i) {
+          if (--st < 0) {
+            st = C::NS - 1;
+            ph ^= 1;
+          }
+          Ctl drain_ctl{abort_flag, p.status, 100000000ull};
+          const uint32_t a = smem_u32(&full[st]);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < drain_ctl.timeout_ns) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_1 = idesc_bf16(kBM, B, false, W_MN);
+      constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool alive = true;
+      bool issued_any = false;
+      int i = 0;
+      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x, ++i) {
+        const int r = u % p.R;
+        const int buf = i & 1;
+        const uint32_t use = uint32_t(i >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + uint32_t(buf * C::ACC_COLS);
+        const uint32_t d1 = d0 + B;
+        const int n = p.counts[r] & 0xFFFF;
+        const uint32_t* plan = p.plan + size_t(r) * p.S;
+        uint32_t init0 = 0, init1 = 0;
+        for (int s = 0; s < n && alive; ++s) {
+          const uint32_t e = plan[s];
+          const bool has0 = ((e >> 16) & 0xFFu) != kNone;
+          const bool has1 = GU && (e >> 24) != kNone;
+          for (int kc = 0; kc < B / kBK; ++kc) {
+            if (!mbar_wait(&full[stage], phase, ctl)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+            const uint32_t w0_addr = a_addr + C::A_BYTES;
+            const uint32_t w1_addr = w0_addr + C::W_BYTES;
+            const bool fused = GU && has0 && has1 && (init0 == init1);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t adesc = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+              if (fused) {
+                mma_bf16(d0, adesc, w_desc<B, W_MN>(w0_addr, kk), IDESC_2, (kk > 0) ? 1u : init0);
+              } else {
+                if (has0) mma_bf16(d0, adesc, w_desc<B, W_MN>(w0_addr, kk), IDESC_1, (kk > 0) ? 1u : init0);
+                if (has1) mma_bf16(d1, adesc, w_desc<B, W_MN>(w1_addr, kk), IDESC_1, (kk > 0) ? 1u : init1);
+              }
+            }
+            issued_any = true;
+            if (has0) init0 = 1;
+            if (has1) init1 = 1;
+            mma_commit(&empty[stage]);
+            if (++stage == C::NS) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+        if (!alive) break;
+        mma_commit(&acc_full[buf]);
+      }
+      if (!alive && issued_any) {
+        // drain: wait (bounded) for every MMA issued so far
+        mma_commit(drain);
+        const uint32_t a = smem_u32(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int i = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
+      const int m = u / p.R, r = u % p.R;
+      const int buf = i & 1;
+      const uint32_t use = uint32_t(i >> 1);
+      if (!mbar_wait(&acc_full[buf], use & 1u, ctl)) break;
+      tc_fence_after();
+      const int cw = p.counts[r];
+      const bool any0 = (cw >> 16) & 1;
+      const bool any1 = (cw >> 17) & 1;
+      const int64_t row = int64_t(m) * kBM + q * 32 + lane;
+      const bool row_ok = row < p.T;
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * C::ACC_COLS);
+#pragma unroll 1
+      for (int j = 0; j < B / 32; ++j) {
+        if constexpr (GU) {
+          uint32_t g[32], v[32];
+          tmem_ld32(tbase + j * 32, g);
+          tmem_ld32(tbase + B + j * 32, v);
+          tmem_ld_wait();
+          uint32_t hp[16], gp[16], up[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const float g0 = any0 ? __uint_as_float(g[2 * t]) : 0.f;
+            const float g1 = any0 ? __uint_as_float(g[2 * t + 1]) : 0.f;
+            const float u0 = any1 ? __uint_as_float(v[2 * t]) : 0.f;
+            const float u1 = any1 ? __uint_as_float(v[2 * t + 1]) : 0.f;
+            hp[t] = pack_bf16x2(silu_fast(g0) * u0, silu_fast(g1) * u1);
+            gp[t] = pack_bf16x2(g0, g1);
+            up[t] = pack_bf16x2(u0, u1);
+          }
+          if (row_ok) {
+            const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
+            __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(p.out) + off;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) st_global_v4(hrow + t * 8, hp[4 * t], hp[4 * t + 1], hp[4 * t + 2], hp[4 * t + 3]);
+            if (p.gate_pre) {
+              __nv_bfloat16* grow = static_cast<__nv_bfloat16*>(p.gate_pre) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                st_global_v4(grow + t * 8, gp[4 * t], gp[4 * t + 1], gp[4 * t + 2], gp[4 * t + 3]);
+            }
+            if (p.up_out) {
+              __nv_bfloat16* urow = static_cast<__nv_bfloat16*>(p.up_out) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                st_global_v4(urow + t * 8, up[4 * t], up[4 * t + 1], up[4 * t + 2], up[4 * t + 3]);
+            }
+          }
+        } else {
+          uint32_t a[32];
+          tmem_ld32(tbase + j * 32, a);
+          tmem_ld_wait();
+          float f[32];
+#pragma unroll
+          for (int t = 0; t < 32; ++t) f[t] = any0 ? __uint_as_float(a[t]) : 0.f;
+          if (row_ok) {
+            const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
+            if (p.add_residual) {
+              const __nv_bfloat16* rrow = static_cast<const __nv_bfloat16*>(p.residual) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const uint4 rv = ld_global_v4(rrow + t * 8);
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                  const float2 x2 = unpack_bf16x2(rw[w]);
+                  f[8 * t + 2 * w] += x2.x;
+                  f[8 * t + 2 * w + 1] += x2.y;
+                }
+              }
+            }
+            if (p.out_f32) {
+              float* orow = static_cast<float*>(p.out) + off;
+#pragma unroll
+              for (int t = 0; t < 8; ++t)
+                st_global_v4(orow + t * 4, __float_as_uint(f[4 * t]), __float_as_uint(f[4 * t + 1]),
+                             __float_as_uint(f[4 * t + 2]), __float_as_uint(f[4 * t + 3]));
+            } else {
+              __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                st_global_v4(orow + t * 8, pack_bf16x2(f[8 * t], f[8 * t + 1]), pack_bf16x2(f[8 * t + 2], f[8 * t + 3]),
+                             pack_bf16x2(f[8 * t + 4], f[8 * t + 5]), pack_bf16x2(f[8 * t + 6], f[8 * t + 7]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- host
+
+struct EllArgs {
+  const BellEll* e;
+  const char* name;
+};
+
+static int check_ell(const BellEll& e, const char* name) {
+  if (!e.values || !e.col_indices) return fail(BELL_ERR_ARG, std::string(name) + ": NULL values/col_indices");
+  if (e.R < 1 || e.C < 1 || e.K < 1) return fail(BELL_ERR_SHAPE, std::string(name) + ": R, C, K must be >= 1");
+  if (e.B != 64 && e.B != 128) return fail(BELL_ERR_SHAPE, std::string(name) + ": tile size B must be 64 or 128");
+  if (e.K > 254) return fail(BELL_ERR_SHAPE, std::string(name) + ": K must be <= 254");
+  if (e.C > 65535) return fail(BELL_ERR_SHAPE, std::string(name) + ": C must be <= 65535");
+  if (e.layout != BELL_TILE_IN_OUT && e.layout != BELL_TILE_OUT_IN)
+    return fail(BELL_ERR_ARG, std::string(name) + ": unknown tile layout");
+  if (!aligned16(e.values)) return fail(BELL_ERR_ALIGN, std::string(name) + ": values not 16-byte aligned");
+  return BELL_OK;
+}
+
+// Weight tensor map: values [R, K, B, B] viewed as 2-D [R*K*B rows, B cols].
+static int make_w_map(CUtensorMap* m, const BellEll& e) {
+  const uint64_t rows = uint64_t(e.R) * uint64_t(e.K) * uint64_t(e.B);
+  if (e.layout == BELL_TILE_IN_OUT)
+    return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, 64, Swz::B128);
+  return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, e.B, Swz::B128);
+}
+
+template <int B, bool GU, bool W_MN>
+static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p,
+                       cudaStream_t stream) {
+  using C = Cfg<B, GU>;
+  auto kern = bell_bf16_kernel<B, GU, W_MN>;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const int64_t units = int64_t(p.n_mtiles) * p.R;
+  if (units == 0) return BELL_OK;
+  const int grid = int(units < sms ? units : sms);
+  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(a, w0, w1, p);
+  return check_launch(GU ? "bell gate/up kernel" : "bell linear kernel");
+}
+
+template <bool GU>
+static int dispatch_bf16(int B, int layout, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
+                         const Bf16Params& p, cudaStream_t s) {
+  const bool mn = layout == BELL_TILE_IN_OUT;
+  if (B == 64) return mn ? launch_bf16<64, GU, true>(a, w0, w1, p, s) : launch_bf16<64, GU, false>(a, w0, w1, p, s);
+  return mn ? launch_bf16<128, GU, true>(a, w0, w1, p, s) : launch_bf16<128, GU, false>(a, w0, w1, p, s);
+}
+
+int check_ffn(const BellFFNDesc* d, int dtype) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (d->dtype != dtype) return fail(BELL_ERR_DTYPE, "descriptor dtype does not match the entry point");
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (int rc = check_ell(d->gate, "gate")) return rc;
+  if (int rc = check_ell(d->up, "up")) return rc;
+  if (int rc = check_ell(d->down, "down")) return rc;
+  const BellEll &g = d->gate, &u = d->up, &w = d->down;
+  if (g.B != u.B || g.B != w.B) return fail(BELL_ERR_SHAPE, "gate, up and down must share the tile size");
+  if (g.R != u.R) return fail(BELL_ERR_SHAPE, "gate and up must have same R_ff");
+  if (g.C != u.C) return fail(BELL_ERR_SHAPE, "gate and up must have the same number of input column blocks");
+  if (g.layout != u.layout) return fail(BELL_ERR_SHAPE, "gate and up must use the same tile layout");
+  if (int64_t(g.C) * g.B != d->d_model) return fail(BELL_ERR_SHAPE, "gate C*B inconsistent with d_model");
+  if (int64_t(g.R) * g.B != d->d_ff) return fail(BELL_ERR_SHAPE, "gate R*B inconsistent with d_ff");
+  if (int64_t(w.R) * w.B != d->d_model)
+    return fail(BELL_ERR_SHAPE, "values_down R_model=" + std::to_string(w.R) + " inconsistent with d_model=" +
+                                    std::to_string(d->d_model));
+  if (int64_t(w.C) * w.B != d->d_ff) return fail(BELL_ERR_SHAPE, "down C*B inconsistent with d_ff");
+  if (!d->x || !d->h || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, h, out and plan must be non-NULL");
+  if (!aligned16(d->x) || !aligned16(d->h) || !aligned16(d->out) || !aligned16(d->plan))
+    return fail(BELL_ERR_ALIGN, "x, h, out and plan must be 16-byte aligned");
+  if ((d->gate_pre && !aligned16(d->gate_pre)) || (d->up_out && !aligned16(d->up_out)) ||
+      (d->residual && !aligned16(d->residual)))
+    return fail(BELL_ERR_ALIGN, "optional buffers must be 16-byte aligned");
+  if (d->T > (int64_t(1) << 31) - 256) return fail(BELL_ERR_SHAPE, "T too large");
+  return BELL_OK;
+}
+
+int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
+  const BellEll &g = d->gate, &u = d->up;
+  CUtensorMap ma, mg, mu;
+  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64, kBM, Swz::B128))
+    return rc;
+  if (int rc = make_w_map(&mg, g)) return rc;
+  if (int rc = make_w_map(&mu, u)) return rc;
+  PlanLayout L = plan_layout(g.R, g.K, u.K, d->down.R, d->down.K);
+  Bf16Params p{};
+  p.T = d->T;
+  p.n_mtiles = int32_t((d->T + kBM - 1) / kBM);
+  p.R = g.R;
+  p.K0 = g.K;
+  p.K1 = u.K;
+  p.S = g.K + u.K;
+  p.plan = reinterpret_cast<const uint32_t*>(static_cast<const char*>(d->plan) + L.gu_entries);
+  p.counts = reinterpret_cast<const int32_t*>(static_cast<const char*>(d->plan) + L.gu_counts);
+  p.out = d->h;
+  p.ld_out = d->d_ff;
+  p.gate_pre = d->gate_pre;
+  p.up_out = d->up_out;
+  p.status = status;
+  p.timeout_ns = wait_budget_ns();
+  return dispatch_bf16<true>(g.B, g.layout, ma, mg, mu, p, s);
+}
+
+int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
+  const BellEll& w = d->down;
+  CUtensorMap ma, mw;
+  if (int rc = make_map_2d(&ma, d->h, MapType::BF16, d->d_ff, d->T, uint64_t(d->d_ff) * 2, 64, kBM, Swz::B128))
+    return rc;
+  if (int rc = make_w_map(&mw, w)) return rc;
+  PlanLayout L = plan_layout(d->gate.R, d->gate.K, d->up.K, w.R, w.K);
+  Bf16Params p{};
+  p.T = d->T;
+  p.n_mtiles = int32_t((d->T + kBM - 1) / kBM);
+  p.R = w.R;
+  p.K0 = w.K;
+  p.K1 = 0;
+  p.S = w.K;
+  p.plan = reinterpret_cast<const uint32_t*>(static_cast<const char*>(d->plan) + L.d_entries);
+  p.counts = reinterpret_cast<const int32_t*>(static_cast<const char*>(d->plan) + L.d_counts);
+  p.out = d->out;
+  p.ld_out = d->d_model;
+  p.residual = d->residual ? d->residual : d->x;
+  p.add_residual = d->add_residual ? 1 : 0;
+  p.out_f32 = 0;
+  p.status = status;
+  p.timeout_ns = wait_budget_ns();
+  return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
+}
+
+}  // namespace bell
+
+using namespace bell;
+
+extern "C" {
+
+int bell_swiglu_fwd_bf16(const BellFFNDesc* d, void* stream) {
+  if (int rc = check_ffn(d, BELL_DTYPE_BF16)) return rc;
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (int rc = launch_plan(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
+                           d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s))
+    return rc;
+  if (int rc = gate_up_bf16(d, status, s)) return rc;
+  return down_bf16(d, status, s);
+}
+
+int bell_gate_up_bf16(const BellFFNDesc* d, void* stream) {
+  if (int rc = check_ffn(d, BELL_DTYPE_BF16)) return rc;
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (int rc = launch_plan(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
+                           d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s))
+    return rc;
+  return gate_up_bf16(d, status, s);
+}
+
+int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (d->dtype != BELL_DTYPE_BF16) return fail(BELL_ERR_DTYPE, "bell_linear_bf16: dtype must be BELL_DTYPE_BF16");
+  if (d->out_dtype != BELL_DTYPE_BF16 && d->out_dtype != BELL_DTYPE_F32)
+    return fail(BELL_ERR_DTYPE, "bell_linear_bf16: out_dtype must be BELL_DTYPE_BF16 or BELL_DTYPE_F32");
+  if (int rc = check_ell(d->w, "weight")) return rc;
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (!d->x || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, out and plan must be non-NULL");
+  if (d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
+  if (!aligned16(d->x) || !aligned16(d->out) || !aligned16(d->plan) || (d->residual && !aligned16(d->residual)))
+    return fail(BELL_ERR_ALIGN, "x, out, residual and plan must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  const BellEll& w = d->w;
+  if (int rc = launch_plan(nullptr, 0, nullptr, 0, 0, 0, w.col_indices, w.K, w.R, w.C, d->plan, status, s)) return rc;
+  const int64_t in_f = int64_t(w.C) * w.B, out_f = int64_t(w.R) * w.B;
+  CUtensorMap ma, mw;
+  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, in_f, d->T, uint64_t(in_f) * 2, 64, kBM, Swz::B128)) return rc;
+  if (int rc = make_w_map(&mw, w)) return rc;
+  PlanLayout L = plan_layout(0, 0, 0, w.R, w.K);
+  Bf16Params p{};
+  p.T = d->T;
+  p.n_mtiles = int32_t((d->T + kBM - 1) / kBM);
+  p.R = w.R;
+  p.K0 = w.K;
+  p.S = w.K;
+  p.plan = reinterpret_cast<const uint32_t*>(static_cast<const char*>(d->plan) + L.d_entries);
+  p.counts = reinterpret_cast<const int32_t*>(static_cast<const char*>(d->plan) + L.d_counts);
+  p.out = d->out;
+  p.ld_out = out_f;
+  p.residual = d->residual;
+  p.add_residual = d->add_residual ? 1 : 0;
+  p.out_f32 = d->out_dtype == BELL_DTYPE_F32 ? 1 : 0;
+  p.status = status;
+  p.timeout_ns = wait_budget_ns();
+  return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
+}
+
+}  // extern "C"

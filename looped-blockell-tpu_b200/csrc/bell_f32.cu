@@ -1,0 +1,268 @@
+// bell_f32.cu — fp32 Block-ELL SwiGLU (accuracy path, rel-L2 <= 1e-5).
+//
+// tcgen05's fp32-input kind (tf32) keeps 10 mantissa bits and cannot meet a
+// 1e-5 relative-L2 target, so this path runs exact fp32 FFMA on CUDA cores:
+// a CTA computes a 64-token x 64-feature output tile, staging 32-wide K
+// chunks of the gathered activation tile and the weight tile(s) in shared
+// memory.  It shares the tile-schedule plan (bell_common.cu) with the bf16
+// path, so dead slots, ragged K and gate/up column merging behave the same.
+// Semantics: looped_blockell/layers/block_ell.py:149-182 and mlp.py:119-145.
+#include <string>
+
+#include "bell_host.h"
+#include "bell_ptx.cuh"
+
+namespace bell {
+
+static constexpr int kTM = 64;   // tokens per CTA
+static constexpr int kTN = 64;   // output features per CTA
+static constexpr int kTK = 32;   // K chunk
+
+struct F32Params {
+  int64_t T;
+  int32_t R, B, K0, K1, S, layout, n_mtiles, n_nchunks;
+  int64_t ld_a, ld_out;
+  const float* a;
+  const float* w0;
+  const float* w1;
+  const uint32_t* plan;
+  const int32_t* counts;
+  float* out;
+  float* gate_pre;
+  float* up_out;
+  const float* residual;
+  int32_t add_residual;
+};
+
+__device__ __forceinline__ void load_w_f32(float (*ws)[kTN + 1], const float* w, int tile, int B, int layout, int kc,
+                                           int n0) {
+  const float* base = w + size_t(tile) * B * B;
+  if (layout == BELL_TILE_IN_OUT) {
+    for (int idx = threadIdx.x; idx < kTK * kTN; idx += blockDim.x) {
+      const int i = idx / kTN, j = idx % kTN;
+      ws[i][j] = base[size_t(kc * kTK + i) * B + n0 + j];
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < kTK * kTN; idx += blockDim.x) {
+      const int j = idx / kTK, i = idx % kTK;
+      ws[i][j] = base[size_t(n0 + j) * B + kc * kTK + i];
+    }
+  }
+}
+
+template <bool GU>
+__global__ void __launch_bounds__(256) bell_f32_kernel(const F32Params p) {
+  __shared__ float xs[kTM][kTK + 1];
+  __shared__ float w0s[kTK][kTN + 1];
+  __shared__ float w1s[GU ? kTK : 1][kTN + 1];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t units = int64_t(p.n_mtiles) * p.R * p.n_nchunks;
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const int nch = int(u % p.n_nchunks);
+    const int r = int((u / p.n_nchunks) % p.R);
+    const int64_t m = u / (int64_t(p.n_nchunks) * p.R);
+    const int n0 = nch * kTN;
+    float acc0[4][4] = {}, acc1[4][4] = {};
+    const int cw = p.counts[r];
+    const int n = cw & 0xFFFF;
+    const uint32_t* plan = p.plan + size_t(r) * p.S;
+    for (int s = 0; s < n; ++s) {
+      const uint32_t e = plan[s];
+      const int c = int(e & 0xFFFFu);
+      const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+      const bool has0 = k0 != 255u, has1 = GU && k1 != 255u;
+      for (int kc = 0; kc < p.B / kTK; ++kc) {
+        for (int idx = tid; idx < kTM * kTK; idx += blockDim.x) {
+          const int i = idx / kTK, k = idx % kTK;
+          const int64_t row = m * kTM + i;
+          xs[i][k] = row < p.T ? p.a[row * p.ld_a + int64_t(c) * p.B + kc * kTK + k] : 0.f;
+        }
+        if (has0) load_w_f32(w0s, p.w0, r * p.K0 + int(k0), p.B, p.layout, kc, n0);
+        if (GU && has1) load_w_f32(w1s, p.w1, r * p.K1 + int(k1), p.B, p.layout, kc, n0);
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < kTK; ++kk) {
+          float a[4], b0[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = xs[ty * 4 + i][kk];
+          if (has0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b0[j] = w0s[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) acc0[i][j] = fmaf(a[i], b0[j], acc0[i][j]);
+          }
+          if constexpr (GU) {
+            if (has1) {
+              float b1[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) b1[j] = w1s[kk][tx * 4 + j];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc1[i][j] = fmaf(a[i], b1[j], acc1[i][j]);
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    const bool any0 = (cw >> 16) & 1, any1 = (cw >> 17) & 1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = m * kTM + ty * 4 + i;
+      if (row >= p.T) continue;
+      const int64_t off = row * p.ld_out + int64_t(r) * p.B + n0 + tx * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (GU) {
+          const float g = any0 ? acc0[i][j] : 0.f;
+          const float v = any1 ? acc1[i][j] : 0.f;
+          p.out[off + j] = g / (1.0f + expf(-g)) * v;
+          if (p.gate_pre) p.gate_pre[off + j] = g;
+          if (p.up_out) p.up_out[off + j] = v;
+        } else {
+          float y = any0 ? acc0[i][j] : 0.f;
+          if (p.add_residual) y += p.residual[off + j];
+          p.out[off + j] = y;
+        }
+      }
+    }
+  }
+}
+
+template <bool GU>
+static int launch_f32(const F32Params& p, cudaStream_t s) {
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const int64_t units = int64_t(p.n_mtiles) * p.R * p.n_nchunks;
+  if (units == 0) return BELL_OK;
+  const int64_t grid = units < int64_t(sms) * 8 ? units : int64_t(sms) * 8;
+  bell_f32_kernel<GU><<<int(grid), 256, 0, s>>>(p);
+  return check_launch(GU ? "bell f32 gate/up kernel" : "bell f32 linear kernel");
+}
+
+static int check_ell_f32(const BellEll& e, const char* name) {
+  if (!e.values || !e.col_indices) return fail(BELL_ERR_ARG, std::string(name) + ": NULL values/col_indices");
+  if (e.R < 1 || e.C < 1 || e.K < 1) return fail(BELL_ERR_SHAPE, std::string(name) + ": R, C, K must be >= 1");
+  if (e.B != 64 && e.B != 128) return fail(BELL_ERR_SHAPE, std::string(name) + ": tile size B must be 64 or 128");
+  if (e.K > 254 || e.C > 65535) return fail(BELL_ERR_SHAPE, std::string(name) + ": K <= 254 and C <= 65535");
+  if (e.layout != BELL_TILE_IN_OUT && e.layout != BELL_TILE_OUT_IN)
+    return fail(BELL_ERR_ARG, std::string(name) + ": unknown tile layout");
+  return BELL_OK;
+}
+
+}  // namespace bell
+
+using namespace bell;
+
+extern "C" {
+
+int bell_swiglu_fwd_f32(const BellFFNDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (d->dtype != BELL_DTYPE_F32) return fail(BELL_ERR_DTYPE, "bell_swiglu_fwd_f32: dtype must be BELL_DTYPE_F32");
+  if (int rc = check_ell_f32(d->gate, "gate")) return rc;
+  if (int rc = check_ell_f32(d->up, "up")) return rc;
+  if (int rc = check_ell_f32(d->down, "down")) return rc;
+  const BellEll &g = d->gate, &u = d->up, &w = d->down;
+  if (g.B != u.B || g.B != w.B) return fail(BELL_ERR_SHAPE, "gate, up and down must share the tile size");
+  if (g.R != u.R || g.C != u.C) return fail(BELL_ERR_SHAPE, "gate and up must have same R_ff and C");
+  if (g.layout != u.layout) return fail(BELL_ERR_SHAPE, "gate and up must use the same tile layout");
+  if (int64_t(g.C) * g.B != d->d_model || int64_t(g.R) * g.B != d->d_ff || int64_t(w.R) * w.B != d->d_model ||
+      int64_t(w.C) * w.B != d->d_ff)
+    return fail(BELL_ERR_SHAPE, "gate/up/down shapes inconsistent with d_model / d_ff");
+  if (!d->x || !d->h || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, h, out and plan must be non-NULL");
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (int rc = launch_plan(g.col_indices, g.K, u.col_indices, u.K, g.R, g.C, w.col_indices, w.K, w.R, w.C, d->plan,
+                           status, s))
+    return rc;
+  PlanLayout L = plan_layout(g.R, g.K, u.K, w.R, w.K);
+  const char* pl = static_cast<const char*>(d->plan);
+  F32Params p{};
+  p.T = d->T;
+  p.R = g.R;
+  p.B = g.B;
+  p.K0 = g.K;
+  p.K1 = u.K;
+  p.S = g.K + u.K;
+  p.layout = g.layout;
+  p.n_mtiles = int32_t((d->T + kTM - 1) / kTM);
+  p.n_nchunks = g.B / kTN;
+  p.ld_a = d->d_model;
+  p.ld_out = d->d_ff;
+  p.a = static_cast<const float*>(d->x);
+  p.w0 = static_cast<const float*>(g.values);
+  p.w1 = static_cast<const float*>(u.values);
+  p.plan = reinterpret_cast<const uint32_t*>(pl + L.gu_entries);
+  p.counts = reinterpret_cast<const int32_t*>(pl + L.gu_counts);
+  p.out = static_cast<float*>(d->h);
+  p.gate_pre = static_cast<float*>(d->gate_pre);
+  p.up_out = static_cast<float*>(d->up_out);
+  if (int rc = launch_f32<true>(p, s)) return rc;
+  F32Params q{};
+  q.T = d->T;
+  q.R = w.R;
+  q.B = w.B;
+  q.K0 = w.K;
+  q.S = w.K;
+  q.layout = w.layout;
+  q.n_mtiles = p.n_mtiles;
+  q.n_nchunks = w.B / kTN;
+  q.ld_a = d->d_ff;
+  q.ld_out = d->d_model;
+  q.a = static_cast<const float*>(d->h);
+  q.w0 = static_cast<const float*>(w.values);
+  q.plan = reinterpret_cast<const uint32_t*>(pl + L.d_entries);
+  q.counts = reinterpret_cast<const int32_t*>(pl + L.d_counts);
+  q.out = static_cast<float*>(d->out);
+  q.residual = static_cast<const float*>(d->residual ? d->residual : d->x);
+  q.add_residual = d->add_residual ? 1 : 0;
+  return launch_f32<false>(q, s);
+}
+
+int bell_linear_f32(const BellLinearDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (d->dtype != BELL_DTYPE_F32 || d->out_dtype != BELL_DTYPE_F32)
+    return fail(BELL_ERR_DTYPE, "bell_linear_f32: dtype and out_dtype must be BELL_DTYPE_F32");
+  if (int rc = check_ell_f32(d->w, "weight")) return rc;
+  if (!d->x || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, out and plan must be non-NULL");
+  if (d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  const BellEll& w = d->w;
+  if (int rc = launch_plan(nullptr, 0, nullptr, 0, 0, 0, w.col_indices, w.K, w.R, w.C, d->plan, status, s)) return rc;
+  PlanLayout L = plan_layout(0, 0, 0, w.R, w.K);
+  const char* pl = static_cast<const char*>(d->plan);
+  F32Params q{};
+  q.T = d->T;
+  q.R = w.R;
+  q.B = w.B;
+  q.K0 = w.K;
+  q.S = w.K;
+  q.layout = w.layout;
+  q.n_mtiles = int32_t((d->T + kTM - 1) / kTM);
+  q.n_nchunks = w.B / kTN;
+  q.ld_a = int64_t(w.C) * w.B;
+  q.ld_out = int64_t(w.R) * w.B;
+  q.a = static_cast<const float*>(d->x);
+  q.w0 = static_cast<const float*>(w.values);
+  q.plan = reinterpret_cast<const uint32_t*>(pl + L.d_entries);
+  q.counts = reinterpret_cast<const int32_t*>(pl + L.d_counts);
+  q.out = static_cast<float*>(d->out);
+  q.residual = static_cast<const float*>(d->residual);
+  q.add_residual = d->add_residual ? 1 : 0;
+  return launch_f32<false>(q, s);
+}
+
+}  // extern "C"

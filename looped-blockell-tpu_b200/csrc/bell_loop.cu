@@ -1,0 +1,155 @@
+// bell_loop.cu — RMSNorm, diagonal SSM injection and the L-iteration
+// shared-weight loop  h <- h + FFN(RMSNorm(h))  (bf16).
+//
+// Loop order follows the reference persistent_mlp_step
+// (csrc/loop/persistent_core.cu:315-335): normalise, run the Block-ELL
+// SwiGLU without fused residual, add the PRE-norm h.  RMSNorm follows
+// looped_blockell/layers/norms.py:8-15 (eps default 1e-5, config.py:110).
+#include <string>
+
+#include "bell_host.h"
+#include "bell_ptx.cuh"
+
+namespace bell {
+
+// One warp per token row; fp32 sum of squares, bf16 in/out.
+__global__ void __launch_bounds__(256) bell_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ gain,
+                                                           __nv_bfloat16* __restrict__ out, int64_t T, int d,
+                                                           float eps) {
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const __nv_bfloat16* xr = x + row * d;
+  __nv_bfloat16* orow = out + row * d;
+  float ss = 0.f;
+  for (int i = lane * 8; i < d; i += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 f = unpack_bf16x2(w[t]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / float(d) + eps);
+  for (int i = lane * 8; i < d; i += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gain + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t g[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 f = unpack_bf16x2(w[t]);
+      const float2 s = unpack_bf16x2(g[t]);
+      o[t] = pack_bf16x2(f.x * inv * s.x, f.y * inv * s.y);
+    }
+    *reinterpret_cast<uint4*>(orow + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// h = exp(-softplus(log_dt) * exp(log_A)) * h + softplus(log_dt) * e
+// (reference diagonal_injection_kernel, persistent_core.cu:53-83).
+__global__ void __launch_bounds__(256) bell_injection_kernel(const __nv_bfloat16* __restrict__ h,
+                                                             const __nv_bfloat16* __restrict__ e,
+                                                             const float* __restrict__ log_A,
+                                                             const float* __restrict__ log_dt,
+                                                             __nv_bfloat16* __restrict__ out, int64_t n, int d) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int f = int(i % d);
+    const float ldt = log_dt[f];
+    const float dt = ldt > 20.f ? ldt : (ldt < -20.f ? expf(ldt) : log1pf(expf(ldt)));
+    const float decay = expf(-dt * expf(log_A[f]));
+    out[i] = __float2bfloat16(decay * __bfloat162float(h[i]) + dt * __bfloat162float(e[i]));
+  }
+}
+
+int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d, float eps, cudaStream_t s) {
+  if (T == 0) return BELL_OK;
+  const int64_t blocks = (T + 7) / 8;
+  bell_rmsnorm_kernel<<<unsigned(blocks), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                        static_cast<const __nv_bfloat16*>(gain),
+                                                        static_cast<__nv_bfloat16*>(out), T, d, eps);
+  return check_launch("bell_rmsnorm_kernel");
+}
+
+}  // namespace bell
+
+using namespace bell;
+
+extern "C" {
+
+int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gain, float eps, void* out,
+                      void* stream) {
+  if (!x || !gain || !out) return fail(BELL_ERR_ARG, "bell_rmsnorm_bf16: NULL pointer");
+  if (T < 0 || d_model <= 0 || d_model % 8 != 0) return fail(BELL_ERR_SHAPE, "bell_rmsnorm_bf16: d_model % 8 != 0");
+  if (!aligned16(x) || !aligned16(gain) || !aligned16(out)) return fail(BELL_ERR_ALIGN, "bell_rmsnorm_bf16: alignment");
+  if (int rc = require_sm100()) return rc;
+  return launch_rmsnorm(x, gain, out, T, d_model, eps, static_cast<cudaStream_t>(stream));
+}
+
+int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,
+                             const float* log_dt, void* out, void* stream) {
+  if (!h || !e || !log_A || !log_dt || !out) return fail(BELL_ERR_ARG, "bell_diag_injection_bf16: NULL pointer");
+  if (T < 0 || d_model <= 0) return fail(BELL_ERR_SHAPE, "bell_diag_injection_bf16: bad shape");
+  if (int rc = require_sm100()) return rc;
+  const int64_t n = T * d_model;
+  if (n == 0) return BELL_OK;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const int64_t want = (n + 255) / 256;
+  const int grid = int(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
+  bell_injection_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(e), log_A, log_dt,
+      static_cast<__nv_bfloat16*>(out), n, d_model);
+  return check_launch("bell_injection_kernel");
+}
+
+int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (d->L < 0) return fail(BELL_ERR_ARG, "L must be >= 0");
+  if (!d->h_in || !d->h_out || !d->norm_gain || !d->hn || !d->h_mid || !d->plan)
+    return fail(BELL_ERR_ARG, "h_in, h_out, norm_gain, hn, h_mid and plan must be non-NULL");
+  BellFFNDesc f{};
+  f.T = d->T;
+  f.d_model = d->d_model;
+  f.d_ff = d->d_ff;
+  f.dtype = BELL_DTYPE_BF16;
+  f.add_residual = 1;
+  f.x = d->hn;
+  f.residual = d->h_out;
+  f.h = d->h_mid;
+  f.out = d->h_out;
+  f.plan = d->plan;
+  f.gate = d->gate;
+  f.up = d->up;
+  f.down = d->down;
+  f.status = d->status;
+  if (int rc = check_ffn(&f, BELL_DTYPE_BF16)) return rc;
+  if (int rc = require_sm100()) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t bytes = size_t(d->T) * d->d_model * 2;
+  if (d->h_out != d->h_in) {
+    cudaError_t e = cudaMemcpyAsync(d->h_out, d->h_in, bytes, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("loop copy: ") + cudaGetErrorString(e));
+  }
+  if (d->T == 0 || d->L == 0) return BELL_OK;
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (int rc = launch_plan(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
+                           d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s))
+    return rc;
+  for (int it = 0; it < d->L; ++it) {
+    if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
+    if (int rc = gate_up_bf16(&f, status, s)) return rc;
+    // out = h_mid Wd + h (the pre-norm state), written in place over h
+    if (int rc = down_bf16(&f, status, s)) return rc;
+  }
+  return BELL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,111 @@
+"""Block-ELL MLP layers — the reference's Flax modules as torch.nn.Modules.
+
+``BlockELLLinear`` and ``MLPBlock`` keep the constructor arguments and the
+parameter / topology layout of looped_blockell/layers/mlp.py:28-168:
+``values [R, K, B, B]`` ~ N(0, 0.02), ``bias`` zeros, topology buffers
+``col_indices [R, K]`` and ``alive_mask [R, K]``; K = max(1, int(C * density));
+topology seeded from (out_features, in_features), so gate and up share it as
+in the reference (mlp.py:84-95).  Dead tiles (alive_mask False) are passed to
+the kernel as column -1 and skipped, which equals zeroing them (mlp.py:73-77).
+The SwiGLU branch runs the fused sm_100a kernel; like the PyTorch mirror
+(interop/pt_model.py:862-867) its projections carry no bias.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .block_ell import BlockELLConfig, BlockELLTensor, create_random_topology
+
+
+def _topology_seed(out_features: int, in_features: int) -> int:
+    return hash((out_features, in_features)) % 2 ** 31
+
+
+class BlockELLLinear(nn.Module):
+    """Single Block-ELL linear layer (reference mlp.py:28-95)."""
+
+    def __init__(self, out_features: int, in_features: int, tile_size: int = 16, density: float = 1.0,
+                 dtype: torch.dtype = torch.bfloat16, bias: bool = True, device=None):
+        super().__init__()
+        B = tile_size
+        if out_features % B or in_features % B:
+            raise ValueError(f"features ({out_features}, {in_features}) must be divisible by tile_size {B}")
+        self.out_features, self.in_features, self.tile_size, self.density = out_features, in_features, B, density
+        self.dtype = dtype
+        self.R, self.C = out_features // B, in_features // B
+        self.K = max(1, int(self.C * density))
+        self.values = nn.Parameter(torch.randn(self.R, self.K, B, B, device=device) * 0.02)
+        self.bias = nn.Parameter(torch.zeros(out_features, device=device)) if bias else None
+        self.register_buffer("col_indices", self._init_topology().to(device))
+        self.register_buffer("alive_mask", torch.ones(self.R, self.K, dtype=torch.bool, device=device))
+
+    def _init_topology(self) -> torch.Tensor:
+        if self.density >= 1.0:
+            return torch.arange(self.C, dtype=torch.int32).repeat(self.R, 1)[:, :self.K].contiguous()
+        return create_random_topology(self.R, self.C, self.K, _topology_seed(self.out_features, self.in_features))
+
+    @property
+    def config(self) -> BlockELLConfig:
+        return BlockELLConfig(R=self.R, C=self.C, K=self.K, B=self.tile_size)
+
+    def effective_col_indices(self) -> torch.Tensor:
+        """col_indices with dead slots set to -1 (skipped by the kernel)."""
+        return torch.where(self.alive_mask, self.col_indices, torch.full_like(self.col_indices, -1)).to(torch.int32)
+
+    def kernel_values(self) -> torch.Tensor:
+        return self.values.detach().to(self.dtype).contiguous()
+
+    def as_block_ell(self) -> BlockELLTensor:
+        return BlockELLTensor(values=self.kernel_values(), col_indices=self.effective_col_indices(), config=self.config)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        from ..kernels.ops import block_ell_linear
+        lead = x.shape[:-1]
+        y = block_ell_linear(x.reshape(-1, self.in_features).to(self.dtype), self.kernel_values(),
+                             self.effective_col_indices())
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y.reshape(*lead, self.out_features)
+
+
+class MLPBlock(nn.Module):
+    """MLP block on Block-ELL weights (reference mlp.py:98-168).
+
+    SwiGLU: ``w_down(silu(w_gate(x)) * w_up(x))`` as one fused forward;
+    otherwise the GELU MLP ``fc2(gelu(fc1(x)))``.
+    """
+
+    def __init__(self, d_model: int, d_ff: int, use_swiglu: bool = False, dropout: float = 0.0, tile_size: int = 16,
+                 density: float = 1.0, dtype: torch.dtype = torch.bfloat16, device=None):
+        super().__init__()
+        self.d_model, self.d_ff, self.use_swiglu, self.dropout = d_model, d_ff, use_swiglu, dropout
+        self.tile_size, self.density, self.dtype = tile_size, density, dtype
+        kw = dict(tile_size=tile_size, density=density, dtype=dtype, device=device)
+        if use_swiglu:
+            self.w_gate = BlockELLLinear(d_ff, d_model, bias=False, **kw)
+            self.w_up = BlockELLLinear(d_ff, d_model, bias=False, **kw)
+            self.w_down = BlockELLLinear(d_model, d_ff, bias=False, **kw)
+        else:
+            self.fc1 = BlockELLLinear(d_ff, d_model, **kw)
+            self.fc2 = BlockELLLinear(d_model, d_ff, **kw)
+
+    def forward(self, x: torch.Tensor, deterministic: bool = True, residual: bool = False) -> torch.Tensor:
+        if self.use_swiglu:
+            from ..kernels.ops import block_ell_swiglu_fwd
+            lead = x.shape[:-1]
+            x2 = x.reshape(-1, self.d_model).to(self.dtype)
+            out = block_ell_swiglu_fwd(x2, self.w_gate.kernel_values(), self.w_gate.effective_col_indices(),
+                                       self.w_up.kernel_values(), self.w_up.effective_col_indices(),
+                                       self.w_down.kernel_values(), self.w_down.effective_col_indices(),
+                                       add_residual=residual)
+            out = out.reshape(*lead, self.d_model)
+        else:
+            out = self.fc2(F.gelu(self.fc1(x)))
+            if residual:
+                out = out + x
+        if self.dropout > 0.0 and not deterministic:
+            out = F.dropout(out, p=self.dropout, training=True)
+        return out

@@ -1,0 +1,107 @@
+"""fp32 path (rel-L2 <= 1e-5), RMSNorm, injection and the L-iteration loop on
+the B200 vs the CPU oracle."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import GOLDEN
+from gpu_util import make_case, oracle_ffn, to_dev
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-5
+TOL_BF16 = 1e-2
+
+
+def _K():
+    from looped_blockell import kernels as K
+    return K
+
+
+@pytest.mark.parametrize("layout", [O.LAYOUT_IN_OUT, O.LAYOUT_OUT_IN])
+def test_config1_fp32_matches_oracle(layout):
+    """BASELINE config 1 at full size: T=1024, d=512, F=2048, B=64, 25%."""
+    K = _K()
+    c = make_case(1024, 512, 2048, 64, 2, 2, 8, seed=1)
+    dc = to_dev(c, torch.float32, layout)
+    ref = {k: v.astype(np.float64) if not k.startswith("c") else v for k, v in c.items()}
+    for add_res in (False, True):
+        out, h, g, u = K.block_ell_swiglu_fwd_with_intermediate(dc["x"], dc["vg"], dc["cg"], dc["vu"], dc["cu"],
+                                                                 dc["vd"], dc["cd"], add_residual=add_res, layout=layout)
+        ro, rh, rg, ru = oracle_ffn(ref, add_residual=add_res)
+        assert O.rel_l2(out.cpu().numpy(), ro) < TOL_F32
+        assert O.rel_l2(h.cpu().numpy(), rh) < TOL_F32
+
+
+@pytest.mark.parametrize("extra", [{}, {"dead": 3}, {"dup": True}])
+def test_fp32_edge_cases(extra):
+    K = _K()
+    c = make_case(77, 256, 1024, 128, 2, 1, 3, seed=3, **extra)
+    dc = to_dev(c, torch.float32)
+    out = K.block_ell_swiglu_fwd(dc["x"], dc["vg"], dc["cg"], dc["vu"], dc["cu"], dc["vd"], dc["cd"])
+    ref = {k: v.astype(np.float64) if not k.startswith("c") else v for k, v in c.items()}
+    assert O.rel_l2(out.cpu().numpy(), oracle_ffn(ref)[0]) < TOL_F32
+
+
+def test_fp32_golden_fixtures():
+    K = _K()
+    for name in ("swiglu_small", "swiglu_dead"):
+        z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+        dc = to_dev({k: z[k] for k in ("x", "vg", "cg", "vu", "cu", "vd", "cd")}, torch.float32)
+        out = K.block_ell_swiglu_fwd(dc["x"], dc["vg"], dc["cg"], dc["vu"], dc["cu"], dc["vd"], dc["cd"])
+        assert O.rel_l2(out.cpu().numpy(), z["out"]) < TOL_F32
+
+
+def test_rmsnorm_matches_reference_fixture():
+    K = _K()
+    z = np.load(os.path.join(GOLDEN, "rmsnorm.npz"))
+    x = torch.from_numpy(z["x"]).to(torch.bfloat16).cuda()
+    g = torch.from_numpy(z["gain"]).to(torch.bfloat16).cuda()
+    out = K.rmsnorm(x, g, float(z["eps"]))
+    ref = O.rmsnorm(x.float().cpu().numpy(), g.float().cpu().numpy(), float(z["eps"]))
+    assert O.rel_l2(out.float().cpu().numpy(), ref) < 5e-3
+
+
+def test_loop_golden_fixture():
+    K = _K()
+    z = np.load(os.path.join(GOLDEN, "loop.npz"))
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).cuda()  # noqa: E731
+    ci = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    out = K.looped_ffn(bf(z["h0"]), bf(z["gain"]), bf(z["vg"]), ci(z["cg"]), bf(z["vu"]), ci(z["cu"]), bf(z["vd"]),
+                       ci(z["cd"]), L=int(z["L"]), eps=float(z["eps"]))
+    assert O.rel_l2(out.float().cpu().numpy(), z["out"]) < TOL_BF16
+
+
+def test_loop_config4_row_sample():
+    """BASELINE config 4 (L=8, T=8192, d=1024, F=4096, B=64, 25%) vs the oracle
+    on a 512-token sample."""
+    from looped_blockell.synth import CONFIGS, make_ffn
+    K = _K()
+    cfg = CONFIGS[4]
+    c = make_ffn(cfg, device="cuda")
+    gain = torch.ones(cfg.d_model, dtype=torch.bfloat16, device="cuda")
+    out = K.looped_ffn(c["x"], gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L)
+    rows = np.random.default_rng(1).choice(cfg.T, 512, replace=False)
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    ref = O.looped_ffn(f(c["x"])[rows], np.ones(cfg.d_model), (f(c["vg"]), c["cg"].cpu().numpy(), 0),
+                       (f(c["vu"]), c["cu"].cpu().numpy(), 0), (f(c["vd"]), c["cd"].cpu().numpy(), 0), L=cfg.L)
+    assert O.rel_l2(out[torch.from_numpy(rows).cuda()].float().cpu().numpy(), ref) < TOL_BF16
+    assert K.read_status() == 0
+
+
+def test_injection_matches_formula():
+    K = _K()
+    rng = np.random.default_rng(5)
+    h = rng.standard_normal((37, 256)).astype(np.float32)
+    e = rng.standard_normal((37, 256)).astype(np.float32)
+    la = rng.standard_normal(256).astype(np.float32)
+    ld = (rng.standard_normal(256) * 3).astype(np.float32)
+    hb, eb = torch.from_numpy(h).to(torch.bfloat16).cuda(), torch.from_numpy(e).to(torch.bfloat16).cuda()
+    out = K.diagonal_injection(hb, eb, torch.from_numpy(la).cuda(), torch.from_numpy(ld).cuda())
+    dt = np.log1p(np.exp(ld.astype(np.float64)))
+    ref = np.exp(-dt * np.exp(la)) * hb.float().cpu().numpy() + dt * eb.float().cpu().numpy()
+    assert O.rel_l2(out.float().cpu().numpy(), ref) < 5e-3
