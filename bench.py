@@ -151,6 +151,7 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=2048)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     args = ap.parse_args()
     from looped_blockell.synth import CONFIGS
     cfg = CONFIGS[args.config]
@@ -300,7 +301,7 @@ def run_gpu(args, cfg, rank, world):
                                 "peak": tc_peak, "unit": "TFLOP/s", "frac": gu["tflops"] / tc_peak,
                                 "peak_source": f"{peak_src} bf16 burst", "traffic": None,
                                 "kernel_ms": gu["ms"], "whole_step_frac": tflops / world / tc_peak}
-        if world == 1:
+        if world == 1 and not args.no_cpu:
             v, dt = cpu_baseline_sample(cfg, args.cpu_tokens)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                                     "sample": f"{args.cpu_tokens} tokens of {cfg.name} ({dt:.1f} s), numpy "

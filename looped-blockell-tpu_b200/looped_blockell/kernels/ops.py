@@ -52,7 +52,7 @@ def _prep_ell(name, values, cols, dtype):
     if values.dim() != 4:
         raise RuntimeError(f"{name} values must be 4-D [R, K, B, B]")
     if values.dtype != dtype:
-        raise RuntimeError(f"All value tensors must be {str(dtype).replace('torch.', '')}")
+        raise RuntimeError("All value tensors must be " + ("bf16" if dtype == torch.bfloat16 else "fp32"))
     if cols.dtype != torch.int32:
         raise RuntimeError("All col_idx tensors must be int32")
     return values.contiguous(), cols.contiguous()
@@ -106,6 +106,35 @@ def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layo
     with torch.cuda.device(dev):
         _lib.check(fn(C.byref(desc), _stream()), "block_ell_swiglu_fwd")
     return out, h, gate_pre, up_out
+
+
+def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: int = TILE_IN_OUT, h=None):
+    """First half only: ``h = silu(x Wg) * (x Wu)`` (the down weight is only
+    shape-checked).  Used by the d_ff-sharded forward."""
+    lib = _lib.load()
+    _check_cuda("x", x)
+    if x.dim() != 2 or x.dtype != torch.bfloat16:
+        raise RuntimeError("x must be 2D bf16")
+    x = x.contiguous()
+    vg, cg = _prep_ell("gate", v_gate, ci_gate, torch.bfloat16)
+    vu, cu = _prep_ell("up", v_up, ci_up, torch.bfloat16)
+    vd, cd = _prep_ell("down", v_down, ci_down, torch.bfloat16)
+    N, d_model = x.shape
+    B = vg.shape[2]
+    d_ff = vg.shape[0] * B
+    if h is None:
+        h = torch.empty((N, d_ff), dtype=torch.bfloat16, device=x.device)
+    plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
+                       dtype=torch.uint8, device=x.device)
+    desc = _lib.BellFFNDesc()
+    desc.T, desc.d_model, desc.d_ff, desc.dtype = N, d_model, d_ff, _lib.BELL_DTYPE_BF16
+    desc.x, desc.h, desc.out, desc.plan = x.data_ptr(), h.data_ptr(), h.data_ptr(), plan.data_ptr()
+    desc.gate = _ell(vg, cg, d_model // B, layout)
+    desc.up = _ell(vu, cu, d_model // B, layout)
+    desc.down = _ell(vd, cd, d_ff // vd.shape[2], layout)
+    with torch.cuda.device(x.device):
+        _lib.check(lib.bell_gate_up_bf16(C.byref(desc), _stream()), "block_ell_gate_up")
+    return h
 
 
 def block_ell_swiglu_fwd(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual: bool = False,
