@@ -148,6 +148,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=5)
     ap.add_argument("--shared-gate-up", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="override T (profiling on a smaller case)")
     ap.add_argument("--ref-tokens", type=int, default=2048)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
@@ -155,6 +156,9 @@ def main():
     args = ap.parse_args()
     from looped_blockell.synth import CONFIGS
     cfg = CONFIGS[args.config]
+    if args.tokens:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, T=args.tokens, name=f"{cfg.name}_T{args.tokens}")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

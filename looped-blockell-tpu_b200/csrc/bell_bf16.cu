@@ -260,7 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = u / p.R, r = u % p.R;
       const int buf = i & 1;
       const uint32_t use = uint32_t(i >> 1);
-      if (!mbar_wait(&acc_full[buf], use & 1u, ctl)) break;
+      const bool got = mbar_wait(&acc_full[buf], use & 1u, ctl);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
       tc_fence_after();
       const int cw = p.counts[r];
       const bool any0 = (cw >> 16) & 1;
@@ -275,33 +276,42 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tbase + j * 32, g);
           tmem_ld32(tbase + B + j * 32, v);
           tmem_ld_wait();
-          uint32_t hp[16], gp[16], up[16];
+          if (!any0 || !any1) {  // a projection with no live tile is zero, so is h
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              if (!any0) g[t] = 0u;
+              if (!any1) v[t] = 0u;
+            }
+          }
+          uint32_t hp[16];
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
-            const float g0 = any0 ? __uint_as_float(g[2 * t]) : 0.f;
-            const float g1 = any0 ? __uint_as_float(g[2 * t + 1]) : 0.f;
-            const float u0 = any1 ? __uint_as_float(v[2 * t]) : 0.f;
-            const float u1 = any1 ? __uint_as_float(v[2 * t + 1]) : 0.f;
+            const float g0 = __uint_as_float(g[2 * t]), g1 = __uint_as_float(g[2 * t + 1]);
+            const float u0 = __uint_as_float(v[2 * t]), u1 = __uint_as_float(v[2 * t + 1]);
             hp[t] = pack_bf16x2(silu_fast(g0) * u0, silu_fast(g1) * u1);
-            gp[t] = pack_bf16x2(g0, g1);
-            up[t] = pack_bf16x2(u0, u1);
           }
           if (row_ok) {
             const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
             __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(p.out) + off;
 #pragma unroll
             for (int t = 0; t < 4; ++t) st_global_v4(hrow + t * 8, hp[4 * t], hp[4 * t + 1], hp[4 * t + 2], hp[4 * t + 3]);
-            if (p.gate_pre) {
+            if (p.gate_pre) {  // optional intermediates: packed only when requested
               __nv_bfloat16* grow = static_cast<__nv_bfloat16*>(p.gate_pre) + off;
 #pragma unroll
               for (int t = 0; t < 4; ++t)
-                st_global_v4(grow + t * 8, gp[4 * t], gp[4 * t + 1], gp[4 * t + 2], gp[4 * t + 3]);
+                st_global_v4(grow + t * 8, pack_bf16x2(__uint_as_float(g[8 * t]), __uint_as_float(g[8 * t + 1])),
+                             pack_bf16x2(__uint_as_float(g[8 * t + 2]), __uint_as_float(g[8 * t + 3])),
+                             pack_bf16x2(__uint_as_float(g[8 * t + 4]), __uint_as_float(g[8 * t + 5])),
+                             pack_bf16x2(__uint_as_float(g[8 * t + 6]), __uint_as_float(g[8 * t + 7])));
             }
             if (p.up_out) {
               __nv_bfloat16* urow = static_cast<__nv_bfloat16*>(p.up_out) + off;
 #pragma unroll
               for (int t = 0; t < 4; ++t)
-                st_global_v4(urow + t * 8, up[4 * t], up[4 * t + 1], up[4 * t + 2], up[4 * t + 3]);
+                st_global_v4(urow + t * 8, pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
+                             pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
+                             pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
+                             pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
             }
           }
         } else {

@@ -189,6 +189,7 @@ struct PlanArgs {
   uint32_t* d_entries;
   int32_t* d_counts;
   int32_t* status;
+  int32_t merge;  // 1: share a step between a gate slot and an up slot on the same column
 };
 
 __global__ void __launch_bounds__(128) bell_plan_kernel(PlanArgs a) {
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(128) bell_plan_kernel(PlanArgs a) {
         continue;
       }
       uint32_t m = 255;
-      for (int j = 0; j < a.K_u; ++j) {
+      for (int j = 0; j < a.K_u && a.merge; ++j) {
         if ((used[j >> 5] >> (j & 31)) & 1u) continue;
         if (cu[j] == c) {
           m = j;
@@ -254,8 +255,15 @@ __global__ void __launch_bounds__(128) bell_plan_kernel(PlanArgs a) {
 int launch_plan(const int32_t* ci_g, int32_t K_g, const int32_t* ci_u, int32_t K_u, int32_t R_gu, int32_t C_gu,
                 const int32_t* ci_d, int32_t K_d, int32_t R_d, int32_t C_d, void* plan, int32_t* status,
                 cudaStream_t stream) {
+  return launch_plan_ex(ci_g, K_g, ci_u, K_u, R_gu, C_gu, ci_d, K_d, R_d, C_d, plan, status, stream, 1);
+}
+
+int launch_plan_ex(const int32_t* ci_g, int32_t K_g, const int32_t* ci_u, int32_t K_u, int32_t R_gu, int32_t C_gu,
+                   const int32_t* ci_d, int32_t K_d, int32_t R_d, int32_t C_d, void* plan, int32_t* status,
+                   cudaStream_t stream, int32_t merge) {
   PlanLayout L = plan_layout(R_gu, K_g, K_u, R_d, K_d);
   PlanArgs a;
+  a.merge = merge;
   a.ci_g = ci_g;
   a.ci_u = ci_u;
   a.ci_d = ci_d;

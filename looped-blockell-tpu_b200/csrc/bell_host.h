@@ -50,6 +50,11 @@ PlanLayout plan_layout(int32_t R_gu, int32_t K_g, int32_t K_u, int32_t R_d, int3
 int launch_plan(const int32_t* ci_g, int32_t K_g, const int32_t* ci_u, int32_t K_u, int32_t R_gu,
                 int32_t C_gu, const int32_t* ci_d, int32_t K_d, int32_t R_d, int32_t C_d, void* plan,
                 int32_t* status, cudaStream_t stream);
+// merge = 0: gate slots then up slots, each in ascending slot order, never
+// sharing a step (the ternary path needs that exact per-matrix order).
+int launch_plan_ex(const int32_t* ci_g, int32_t K_g, const int32_t* ci_u, int32_t K_u, int32_t R_gu,
+                   int32_t C_gu, const int32_t* ci_d, int32_t K_d, int32_t R_d, int32_t C_d, void* plan,
+                   int32_t* status, cudaStream_t stream, int32_t merge);
 
 // bf16 building blocks (bell_bf16.cu): descriptor checks, the gate/up launch
 // and the down (linear + residual) launch, on an already-built plan.

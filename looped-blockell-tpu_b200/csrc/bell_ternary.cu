@@ -1,11 +1,467 @@
-// bell_ternary.cu — ternary (2-bit weights, int8 activations) Block-ELL SwiGLU.
+// bell_ternary.cu — ternary Block-ELL SwiGLU: 2-bit packed {-1,0,+1} tiles
+// with one fp32 scale per tile, int8 per-token activations, exact int32 tile
+// products on tcgen05 (kind::i8), fp32 scale-accumulation in ascending slot
+// order.  No reference kernel exists; the arithmetic restates
+// bonsai-test/bitlinear.py:34-69 (AbsMean weights, absmax activations,
+// Qb = 128, clamp [-128, 127]) with the tile as the weight group.
+//
+// Pipeline of one forward:
+//   1. quantise x per token            -> q_x int8, s_x = 128 / absmax
+//   2. gate/up kernel: I_k = q_x . t_k (int32, TMEM), acc += s_k * I_k
+//      (fp32, ascending k), gate = acc / s_x, h = silu(gate) * up (fp32),
+//      per-token |h| max via atomicMax
+//   3. quantise h with that max         -> q_h int8, s_h
+//   4. down kernel: same tile products on q_h, out = acc / s_h (+ x)
+// Arithmetic that must match the CPU oracle bit for bit uses explicit
+// round-to-nearest intrinsics (no FMA contraction).
+#include <string>
+
 #include "bell_host.h"
 #include "bell_ptx.cuh"
 
+namespace bell {
+namespace tern {
+
+static constexpr int kB = 64;        // tile size supported by the ternary path
+static constexpr int kBM = 128;      // tokens per unit
+static constexpr int kA = kBM * kB;  // int8 activation tile bytes (8 KB)
+static constexpr int kW = kB * kB;   // unpacked int8 weight tile bytes (4 KB)
+static constexpr int kStage = 12288; // A + W, 1024-aligned
+static constexpr int kNS = 12;
+static constexpr int kSlots = 8;     // TMEM result slots of 64 columns
+static constexpr int kThreads = 448; // 14 warps
+static constexpr int kSmem = kNS * kStage + 1024 + 1024;
+
+// ------------------------------------------------------------ quantisation
+
+// One warp per token row.  absmax = max|v| (clamped to 1e-8),
+// scale = 128 / absmax, q = clamp(rint(v * scale), -128, 127).  When
+// `absmax_in` is given (bit patterns of a non-negative float per row, as
+// left by atomicMax), it replaces the row scan.  `scale_out` may alias
+// `absmax_in`: every lane reads before lane 0 writes.
+template <typename Tin>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const Tin* __restrict__ in, int8_t* __restrict__ q,
+                                                        float* scale_out, const uint32_t* absmax_in, int64_t T,
+                                                        int d) {
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const Tin* r = in + row * d;
+  float amax;
+  if (absmax_in) {
+    amax = __uint_as_float(absmax_in[row]);
+  } else {
+    amax = 0.f;
+    for (int i = lane; i < d; i += 32) {
+      float v;
+      if constexpr (sizeof(Tin) == 2) v = __bfloat162float(r[i]);
+      else v = r[i];
+      amax = fmaxf(amax, fabsf(v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  }
+  amax = fmaxf(amax, 1e-8f);
+  const float scale = __fdiv_rn(128.0f, amax);
+  __syncwarp();
+  if (lane == 0) scale_out[row] = scale;
+  int8_t* qr = q + row * d;
+  for (int i = lane * 4; i < d; i += 128) {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float v;
+      if constexpr (sizeof(Tin) == 2) v = __bfloat162float(r[i + t]);
+      else v = r[i + t];
+      int qi = __float2int_rn(__fmul_rn(v, scale));
+      qi = qi < -128 ? -128 : (qi > 127 ? 127 : qi);
+      packed |= (uint32_t(qi) & 0xFFu) << (8 * t);
+    }
+    *reinterpret_cast<uint32_t*>(qr + i) = packed;
+  }
+}
+
+// Expand 16 two-bit codes (one packed word) to 16 int8 values:
+// code 00 -> 0, 01 -> +1, 11 -> -1.
+__device__ __forceinline__ uint4 unpack16(uint32_t w) {
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t b = (w >> (8 * q)) & 0xFFu;
+    uint32_t s = (b & 3u) | ((b & 0xCu) << 6) | ((b & 0x30u) << 12) | ((b & 0xC0u) << 18);
+    s |= ((s >> 1) & 0x01010101u) * 0xFEu;  // sign-extend the 2-bit fields (11 -> 0xFF)
+    o[q] = s;
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+struct TernParams {
+  int64_t T;
+  int32_t n_mtiles, R, K0, K1, S;
+  const uint32_t* plan;
+  const int32_t* counts;
+  const uint8_t* packed0;  // gate (or down) packed tiles
+  const uint8_t* packed1;  // up packed tiles
+  const float* scales0;
+  const float* scales1;
+  const float* tok_scale;  // s_x (GU) or s_h (down): 128 / absmax
+  float* out;              // GU: h [T, R*64]; down: out [T, R*64]
+  int64_t ld_out;
+  float* gate_pre;         // GU optional
+  float* up_out;           // GU optional
+  uint32_t* absmax_h;      // GU: per-token max |h| (float bits)
+  const __nv_bfloat16* residual;  // down: x when adding the residual
+  int32_t* status;
+  uint64_t timeout_ns;
+};
+
+// Warp roles: 0 TMA producer (activation tiles), 1 TMEM owner + MMA issuer,
+// 2-5 weight unpackers, 6-13 epilogue (two warps per TMEM lane quadrant, each
+// owning 32 of the 64 result columns).  Every plan step is one (column
+// block, weight tile) pair of ONE matrix; results land in one of 8 TMEM slots
+// of 64 int32 columns and are consumed in plan order.
+template <bool GU>
+__global__ void __launch_bounds__(kThreads, 1)
+    ternary_kernel(const __grid_constant__ CUtensorMap tm_a, const TernParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kNS * kStage);
+  uint64_t* empty = full + kNS;
+  uint64_t* tfull = empty + kNS;
+  uint64_t* tempty = tfull + kSlots;
+  uint64_t* drain = tempty + kSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Ctl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&full[s], 2);  // producer (A bytes) + unpack group
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 8);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_units = p.n_mtiles * p.R;
+
+  if (warp == 0) {
+    if (lane == 0) {  // -------------------------------------------- producer
+      prefetch_tmap(&tm_a);
+      const uint64_t pol = policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool alive = true;
+      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+        const int m = u / p.R, r = u % p.R;
+        const int n = p.counts[r] & 0xFFFF;
+        for (int s = 0; s < n; ++s) {
+          const int c = int(p.plan[size_t(r) * p.S + s] & 0xFFFFu);
+          if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kA);
+          tma_load_2d(smem + stage * kStage, &tm_a, &full[stage], c * kB, m * kBM, pol);
+          if (++stage == kNS) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ----------------------------------------- MMA issuer
+      constexpr uint32_t IDESC = idesc_s8(kBM, kB, false, false);
+      int stage = 0, slot = 0;
+      uint32_t phase = 0, sphase = 0;
+      bool alive = true, any = false;
+      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+        const int r = u % p.R;
+        const int n = p.counts[r] & 0xFFFF;
+        for (int s = 0; s < n && alive; ++s) {
+          if (!mbar_wait(&tempty[slot], sphase ^ 1, ctl) || !mbar_wait(&full[stage], phase, ctl)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * kStage);
+          const uint32_t w_addr = a_addr + kA;
+#pragma unroll
+          for (int kk = 0; kk < kB / 32; ++kk)
+            mma_i8(tmem + uint32_t(slot * kB), sdesc_sw64(a_addr + kk * 32, 16, 512),
+                   sdesc_sw64(w_addr + kk * 32, 16, 512), IDESC, kk > 0 ? 1u : 0u);
+          any = true;
+          mma_commit(&empty[stage]);
+          mma_commit(&tfull[slot]);
+          if (++stage == kNS) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++slot == kSlots) {
+            slot = 0;
+            sphase ^= 1;
+          }
+        }
+      }
+      if (!alive && any) {
+        mma_commit(drain);
+        const uint32_t a = smem_u32(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------- weight unpack
+    const int t = threadIdx.x - 64;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int r = u % p.R;
+      const int n = p.counts[r] & 0xFFFF;
+      bool alive = true;
+      for (int s = 0; s < n; ++s) {
+        const uint32_t e = p.plan[size_t(r) * p.S + s];
+        const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+        const uint8_t* src = (k0 != 255u) ? p.packed0 + (size_t(r) * p.K0 + k0) * (kB * kB / 4)
+                                          : p.packed1 + (size_t(r) * p.K1 + k1) * (kB * kB / 4);
+        mbar_wait(&empty[stage], phase ^ 1, ctl);
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // one abort decision for the whole group
+        if (*abort_flag) {
+          alive = false;
+          break;
+        }
+        uint8_t* w = smem + stage * kStage + kA;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {  // 256 words per tile, 2 per thread
+          const int widx = t + i * 128;
+          const int nrow = widx >> 2, c = widx & 3;
+          const uint32_t word = __ldg(reinterpret_cast<const uint32_t*>(src) + widx);
+          *reinterpret_cast<uint4*>(w + nrow * 64 + ((c ^ ((nrow >> 1) & 3)) << 4)) = unpack16(word);
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (t == 0) mbar_arrive(&full[stage]);
+        if (++stage == kNS) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!alive) break;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3, half = (warp - 6) >> 2;
+    int slot = 0;
+    uint32_t sphase = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int m = u / p.R, r = u % p.R;
+      const int n = p.counts[r] & 0xFFFF;
+      float acc0[32], acc1[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc0[j] = acc1[j] = 0.f;
+      bool alive = true;
+      for (int s = 0; s < n; ++s) {
+        const uint32_t e = p.plan[size_t(r) * p.S + s];
+        const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+        const bool is0 = k0 != 255u;
+        const float sc = is0 ? p.scales0[size_t(r) * p.K0 + k0] : p.scales1[size_t(r) * p.K1 + k1];
+        const bool got = mbar_wait(&tfull[slot], sphase, ctl);
+        if (!__all_sync(0xffffffffu, got)) {  // warp-uniform before the collective tcgen05.ld
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kB + half * 32), v);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          // exact int32 -> fp32 for |I| < 2^22 (here |I| <= 128 * 64)
+          const float fi = __fsub_rn(__int_as_float(int(v[j]) + 0x4B400000), 12582912.0f);
+          const float prod = __fmul_rn(sc, fi);
+          if (!GU || is0) acc0[j] = __fadd_rn(acc0[j], prod);
+          else acc1[j] = __fadd_rn(acc1[j], prod);
+        }
+        if (++slot == kSlots) {
+          slot = 0;
+          sphase ^= 1;
+        }
+      }
+      if (!alive) break;
+      const int64_t row = int64_t(m) * kBM + q * 32 + lane;
+      if (row < p.T) {
+        const float ts = p.tok_scale[row];
+        const int64_t off = row * p.ld_out + int64_t(r) * kB + half * 32;
+        if constexpr (GU) {
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float hv[4], gv[4], uv[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              gv[t] = __fdiv_rn(acc0[j + t], ts);
+              uv[t] = __fdiv_rn(acc1[j + t], ts);
+              hv[t] = __fmul_rn(__fdiv_rn(gv[t], __fadd_rn(1.0f, expf(-gv[t]))), uv[t]);
+              amax = fmaxf(amax, fabsf(hv[t]));
+            }
+            *reinterpret_cast<float4*>(p.out + off + j) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+            if (p.gate_pre) *reinterpret_cast<float4*>(p.gate_pre + off + j) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            if (p.up_out) *reinterpret_cast<float4*>(p.up_out + off + j) = make_float4(uv[0], uv[1], uv[2], uv[3]);
+          }
+          atomicMax(p.absmax_h + row, __float_as_uint(amax));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float o[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              o[t] = __fdiv_rn(acc0[j + t], ts);
+              if (p.residual) o[t] = __fadd_rn(o[t], __bfloat162float(p.residual[off + j + t]));
+            }
+            *reinterpret_cast<float4*>(p.out + off + j) = make_float4(o[0], o[1], o[2], o[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+static int check_tern(const BellTernaryEll& e, const char* name) {
+  if (!e.packed || !e.scales || !e.col_indices) return fail(BELL_ERR_ARG, std::string(name) + ": NULL pointer");
+  if (e.R < 1 || e.C < 1 || e.K < 1 || e.K > 254 || e.C > 65535)
+    return fail(BELL_ERR_SHAPE, std::string(name) + ": need R, C, K >= 1, K <= 254, C <= 65535");
+  if (e.B != kB) return fail(BELL_ERR_SHAPE, std::string(name) + ": the ternary path supports tile size 64");
+  if (!aligned16(e.packed)) return fail(BELL_ERR_ALIGN, std::string(name) + ": packed tiles not 16-byte aligned");
+  return BELL_OK;
+}
+
+static int launch_quant_bf16(const void* x, int8_t* q, float* s, int64_t T, int d, cudaStream_t st) {
+  quant_rows_kernel<__nv_bfloat16><<<unsigned((T + 7) / 8), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), q, s,
+                                                                         nullptr, T, d);
+  return check_launch("quant_rows_kernel<bf16>");
+}
+
+template <bool GU>
+static int launch_tern(const CUtensorMap& map, const TernParams& p, cudaStream_t st) {
+  auto kern = ternary_kernel<GU>;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), kSmem)) return rc;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const int64_t units = int64_t(p.n_mtiles) * p.R;
+  if (units == 0) return BELL_OK;
+  kern<<<int(units < sms ? units : sms), kThreads, kSmem, st>>>(map, p);
+  return check_launch(GU ? "ternary gate/up kernel" : "ternary down kernel");
+}
+
+}  // namespace tern
+}  // namespace bell
+
 using namespace bell;
+using namespace bell::tern;
 
 extern "C" int bell_swiglu_fwd_ternary(const BellTernaryFFNDesc* d, void* stream) {
-  (void)stream;
   if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
-  return fail(BELL_ERR_DTYPE, "ternary path not available in this build");
+  if (int rc = check_tern(d->gate, "gate")) return rc;
+  if (int rc = check_tern(d->up, "up")) return rc;
+  if (int rc = check_tern(d->down, "down")) return rc;
+  const BellTernaryEll &g = d->gate, &u = d->up, &w = d->down;
+  if (g.R != u.R || g.C != u.C) return fail(BELL_ERR_SHAPE, "gate and up must have same R_ff and C");
+  if (int64_t(g.C) * kB != d->d_model || int64_t(g.R) * kB != d->d_ff || int64_t(w.R) * kB != d->d_model ||
+      int64_t(w.C) * kB != d->d_ff)
+    return fail(BELL_ERR_SHAPE, "gate/up/down shapes inconsistent with d_model / d_ff");
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (!d->x || !d->q_x || !d->s_x || !d->h || !d->q_h || !d->s_h || !d->out || !d->plan)
+    return fail(BELL_ERR_ARG, "x, q_x, s_x, h, q_h, s_h, out and plan must be non-NULL");
+  if (!aligned16(d->x) || !aligned16(d->q_x) || !aligned16(d->q_h) || !aligned16(d->h) || !aligned16(d->out) ||
+      (d->gate_pre && !aligned16(d->gate_pre)) || (d->up_out && !aligned16(d->up_out)))
+    return fail(BELL_ERR_ALIGN, "activation buffers must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (int rc = launch_plan_ex(g.col_indices, g.K, u.col_indices, u.K, g.R, g.C, w.col_indices, w.K, w.R, w.C, d->plan,
+                              status, s, /*merge=*/0))
+    return rc;
+  const PlanLayout L = plan_layout(g.R, g.K, u.K, w.R, w.K);
+  const char* pl = static_cast<const char*>(d->plan);
+  const int32_t n_mtiles = int32_t((d->T + kBM - 1) / kBM);
+
+  // 1. per-token int8 quantisation of x
+  if (int rc = launch_quant_bf16(d->x, d->q_x, d->s_x, d->T, d->d_model, s)) return rc;
+  // 2. gate/up tile products, SiLU*up, per-token max|h| (s_h holds it until step 3)
+  cudaError_t e = cudaMemsetAsync(d->s_h, 0, size_t(d->T) * sizeof(float), s);
+  if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("memset: ") + cudaGetErrorString(e));
+  CUtensorMap mx, mh;
+  if (int rc = make_map_2d(&mx, d->q_x, MapType::INT8, d->d_model, d->T, d->d_model, 64, kBM, Swz::B64)) return rc;
+  TernParams p{};
+  p.T = d->T;
+  p.n_mtiles = n_mtiles;
+  p.R = g.R;
+  p.K0 = g.K;
+  p.K1 = u.K;
+  p.S = g.K + u.K;
+  p.plan = reinterpret_cast<const uint32_t*>(pl + L.gu_entries);
+  p.counts = reinterpret_cast<const int32_t*>(pl + L.gu_counts);
+  p.packed0 = g.packed;
+  p.packed1 = u.packed;
+  p.scales0 = g.scales;
+  p.scales1 = u.scales;
+  p.tok_scale = d->s_x;
+  p.out = d->h;
+  p.ld_out = d->d_ff;
+  p.gate_pre = d->gate_pre;
+  p.up_out = d->up_out;
+  p.absmax_h = reinterpret_cast<uint32_t*>(d->s_h);
+  p.status = status;
+  p.timeout_ns = wait_budget_ns();
+  if (int rc = launch_tern<true>(mx, p, s)) return rc;
+  // 3. per-token int8 quantisation of h with the max found above
+  quant_rows_kernel<float><<<unsigned((d->T + 7) / 8), 256, 0, s>>>(d->h, d->q_h, d->s_h,
+                                                                    reinterpret_cast<const uint32_t*>(d->s_h), d->T,
+                                                                    d->d_ff);
+  if (int rc = check_launch("quant_rows_kernel<f32>")) return rc;
+  // 4. down tile products (+ residual)
+  if (int rc = make_map_2d(&mh, d->q_h, MapType::INT8, d->d_ff, d->T, d->d_ff, 64, kBM, Swz::B64)) return rc;
+  TernParams q{};
+  q.T = d->T;
+  q.n_mtiles = n_mtiles;
+  q.R = w.R;
+  q.K0 = w.K;
+  q.S = w.K;
+  q.plan = reinterpret_cast<const uint32_t*>(pl + L.d_entries);
+  q.counts = reinterpret_cast<const int32_t*>(pl + L.d_counts);
+  q.packed0 = w.packed;
+  q.scales0 = w.scales;
+  q.tok_scale = d->s_h;
+  q.out = d->out;
+  q.ld_out = d->d_model;
+  q.residual = d->add_residual ? static_cast<const __nv_bfloat16*>(d->x) : nullptr;
+  q.status = status;
+  q.timeout_ns = wait_budget_ns();
+  return launch_tern<false>(mh, q, s);
 }

@@ -298,7 +298,9 @@ def ternary_block_ell_matmul(q: np.ndarray, scale: np.ndarray, t: np.ndarray,
     """
     R, K, B, _ = t.shape
     T = q.shape[0]
-    qi = q.astype(np.int64)
+    # integer products via float64 GEMM: every partial sum is an integer
+    # below 2^53, so the result is exact (|I| <= 128 * B)
+    qf = q.astype(np.float64)
     y = np.zeros((T, R * B), dtype=np.float32)
     sums = {} if return_tile_sums else None
     for r in range(R):
@@ -307,7 +309,7 @@ def ternary_block_ell_matmul(q: np.ndarray, scale: np.ndarray, t: np.ndarray,
             c = int(cols[r, k])
             if c < 0:
                 continue
-            I = (qi[:, c * B:(c + 1) * B] @ t[r, k].astype(np.int64)).astype(np.int32)
+            I = np.rint(qf[:, c * B:(c + 1) * B] @ t[r, k].astype(np.float64)).astype(np.int32)
             if sums is not None:
                 sums[(r, k)] = I
             prod = (np.float32(s_w[r, k]) * I.astype(np.float32)).astype(np.float32)
