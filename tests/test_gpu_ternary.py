@@ -46,7 +46,8 @@ def test_ternary_bit_exact_stages(shape, add_residual):
     # weights: the package's quantiser equals the oracle's restatement of bitlinear
     t_ref, s_ref = O.ternary_quantize_tiles(case["vg"])
     np.testing.assert_array_equal(m["g"][0], t_ref)
-    np.testing.assert_allclose(m["g"][1], s_ref, rtol=2e-7, atol=0)
+    # tile means summed in a different order (GPU reduction vs numpy pairwise): a few ulp
+    np.testing.assert_allclose(m["g"][1], s_ref, rtol=1e-6, atol=0)
     # 1. int8 activations and their scale: bit-exact
     q_x, s_x = O.activation_quantize_int(x)
     np.testing.assert_array_equal(ws["q_x"], q_x)
