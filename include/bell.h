@@ -114,6 +114,22 @@ size_t bell_plan_bytes(int32_t R_gu, int32_t K_gate, int32_t K_up, int32_t R_dow
  */
 int bell_swiglu_fwd_bf16(const BellFFNDesc* desc, void* stream);
 
+/*
+ * Same forward for callers that cannot allocate device memory (an FFI host
+ * whose runtime owns all device memory, or a server that sizes its memory
+ * once at start-up).  No counterpart in the reference.  The plan and h come
+ * from a static scratch array inside the library (BELL_NOALLOC_SCRATCH_BYTES,
+ * reserved on every GPU that loads it); desc->h and desc->plan must be NULL.
+ * Rejects problems needing more than that (see bell_noalloc_scratch_bytes)
+ * with BELL_ERR_SHAPE.  The first call on a device looks up the array's
+ * address; make it before any stream capture.  Calls share the array, so
+ * calls that overlap on the GPU race.  Allocates nothing.
+ */
+#define BELL_NOALLOC_SCRATCH_BYTES (32u << 20)
+int bell_swiglu_fwd_bf16_noalloc(const BellFFNDesc* desc, void* stream);
+size_t bell_noalloc_scratch_bytes(int64_t T, int32_t d_ff, int32_t R_gu, int32_t K_gate, int32_t K_up,
+                                  int32_t R_down, int32_t K_down);
+
 /* Gate/up half only: h = silu(x Wg) * (x Wu) (+ gate_pre/up_out).
  * Replaces the reference's first launch, block_ell_gate_up_silu_kernel
  * (swiglu_fwd.cu:140-402, launched at :652). */
