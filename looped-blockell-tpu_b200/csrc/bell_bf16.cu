@@ -73,8 +73,9 @@ __device__ __forceinline__ void load_w_chunk(uint8_t* dst, const CUtensorMap* ma
     for (int nh = 0; nh < B / 64; ++nh)
       tma_load_2d(dst + nh * 8192, map, bar, nh * 64, tile * B + kc * kBK, pol);
   } else {
-    // [B_out, B_in] tile rows are N; one box of 64 K x B rows.
-    tma_load_2d(dst, map, bar, kc * kBK, tile * B, pol);
+    // [B_out, B_in] tile rows are N; boxes of 64 K x 64 rows stacked along N.
+#pragma unroll
+    for (int nb = 0; nb < B / 64; ++nb) tma_load_2d(dst + nb * 8192, map, bar, kc * kBK, tile * B + nb * 64, pol);
   }
 }
 
@@ -367,6 +368,322 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ================================================================ 2-SM kernel
+//
+// B = 128 only.  A cluster of two CTAs works on one unit of 256 tokens x one
+// output block-row; CTA c owns tokens [256m + 128c, +128).  The even CTA
+// issues tcgen05.mma.cta_group::2 with M = 256: A comes from each CTA's own
+// rows, B is split by N — on a shared gate|up step (N = 256) CTA 0 supplies
+// the gate tile and CTA 1 the up tile; on an N = 128 step each CTA supplies
+// 64 columns.  Per CTA, a stage is 16 KB of x plus at most 16 KB of weights,
+// half the weight bytes of the single-CTA kernel, and the MMA reads half the
+// B operand from each CTA's shared memory.  Both CTAs' TMA loads complete on
+// the even CTA's `full` barrier; its MMA commits release the stage and the
+// accumulator in both CTAs; both epilogues free an accumulator by arriving
+// on the even CTA's `acc_empty` (count 8).
+namespace pair {
+
+static constexpr int B = 128;
+static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB of this CTA's 128 token rows
+static constexpr int W_BYTES = kBK * 128 * 2;  // 16 KB: one [64 K x 128 N] box pair
+template <bool GU>
+struct PCfg {
+  static constexpr int STAGE = A_BYTES + W_BYTES;  // 32 KB (linear steps use half of W)
+  static constexpr int NS = 6;
+  static constexpr int ACC_COLS = GU ? 256 : 128;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;
+  static constexpr int SMEM = NS * STAGE + 1024 + 512;
+};
+
+template <bool GU, bool W_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    bell_bf16_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w0,
+                          const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
+  using C = PCfg<GU>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE);
+  uint64_t* empty = full + C::NS;
+  uint64_t* acc_full = empty + C::NS;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  Ctl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int pairs = gridDim.x >> 1, pid = blockIdx.x >> 1;
+  const int n_units = p.n_mtiles * p.R;  // n_mtiles counts 256-token tiles here
+
+  if (warp == 0) {
+    if (lane == 0) {  // -------------------------------------------- producer
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_w0);
+      if (GU) prefetch_tmap(&tm_w1);
+      const uint64_t pol_a = policy_evict_normal(), pol_w = policy_evict_last();
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      bool alive = true;
+      for (int u = pid; u < n_units && alive; u += pairs) {
+        const int m = u / p.R, r = u % p.R;
+        const int n = p.counts[r] & 0xFFFF;
+        const uint32_t* plan = p.plan + size_t(r) * p.S;
+        for (int s = 0; s < n && alive; ++s) {
+          const uint32_t e = plan[s];
+          const int c = int(e & 0xFFFFu);
+          const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+          const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
+          const bool fused = has0 && has1;
+          // both CTAs' bytes land on the even CTA's barrier
+          const uint32_t step_bytes = 2 * A_BYTES + (fused ? 2 * W_BYTES : W_BYTES);
+          for (int kc = 0; kc < B / kBK; ++kc) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
+              alive = false;
+              break;
+            }
+            uint8_t* st = smem + stage * C::STAGE;
+            const uint32_t bar0 = mapa_shared(smem_u32(&full[stage]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], step_bytes);
+            tma_load_2d_pair(st, &tm_a, bar0, c * B + kc * kBK, m * 256 + int(rank) * kBM, pol_a);
+            // this CTA's half of B
+            const CUtensorMap* wm;
+            int tile, n_off, n_len;
+            if (fused) {  // CTA 0: the whole gate tile, CTA 1: the whole up tile
+              wm = rank == 0 ? &tm_w0 : &tm_w1;
+              tile = rank == 0 ? r * p.K0 + int(k0) : r * p.K1 + int(k1);
+              n_off = 0;
+              n_len = 128;
+            } else {  // one tile, columns split 64 / 64
+              wm = has0 ? &tm_w0 : &tm_w1;
+              tile = has0 ? r * p.K0 + int(k0) : r * p.K1 + int(k1);
+              n_off = int(rank) * 64;
+              n_len = 64;
+            }
+            if constexpr (W_MN) {
+              for (int nb = 0; nb < n_len / 64; ++nb)
+                tma_load_2d_pair(st + A_BYTES + nb * 8192, wm, bar0, n_off + nb * 64, tile * B + kc * kBK, pol_w);
+            } else {
+              // [B_out, B_in] tiles: rows are N; box of 64 K x 64 rows, twice for 128 rows
+              for (int nb = 0; nb < n_len / 64; ++nb)
+                tma_load_2d_pair(st + A_BYTES + nb * 8192, wm, bar0, kc * kBK, tile * B + n_off + nb * 64, pol_w);
+            }
+            ++issued;
+            if (++stage == C::NS) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      (void)issued;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {  // --------------------- MMA issuer (even CTA)
+      constexpr uint32_t IDESC_N128 = idesc_bf16(256, 128, false, W_MN);
+      constexpr uint32_t IDESC_N256 = idesc_bf16(256, 256, false, W_MN);
+      int stage = 0, i = 0;
+      uint32_t phase = 0;
+      bool alive = true, issued_any = false;
+      for (int u = pid; u < n_units && alive; u += pairs, ++i) {
+        const int r = u % p.R;
+        const int buf = i & 1;
+        const uint32_t use = uint32_t(i >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + uint32_t(buf * C::ACC_COLS), d1 = d0 + 128;
+        const int n = p.counts[r] & 0xFFFF;
+        const uint32_t* plan = p.plan + size_t(r) * p.S;
+        uint32_t init0 = 0, init1 = 0;
+        for (int s = 0; s < n && alive; ++s) {
+          const uint32_t e = plan[s];
+          const bool has0 = ((e >> 16) & 0xFFu) != kNone;
+          const bool has1 = GU && (e >> 24) != kNone;
+          const bool fused = has0 && has1;
+          for (int kc = 0; kc < B / kBK; ++kc) {
+            if (!mbar_wait(&full[stage], phase, ctl)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + stage * C::STAGE);
+            const uint32_t w_addr = a_addr + A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t adesc = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+              const uint64_t bdesc = W_MN ? sdesc_sw128(w_addr + kk * 2048, 8192, 1024)
+                                          : sdesc_sw128(w_addr + kk * 32, 16, 1024);
+              if (fused) {
+                // The plan lists a row's shared steps before its single ones, so gate and
+                // up are always in the same state here (one N=256 MMA spans both CTAs'
+                // halves and cannot initialise one accumulator and add to the other).
+                mma_bf16_pair(d0, adesc, bdesc, IDESC_N256, kk > 0 ? 1u : init0);
+                if (kk == 0 && init0 != init1) atomicOr(p.status, BELL_STATUS_INTERNAL);
+              } else {
+                mma_bf16_pair(has0 ? d0 : d1, adesc, bdesc, IDESC_N128, kk > 0 ? 1u : (has0 ? init0 : init1));
+              }
+            }
+            issued_any = true;
+            if (has0) init0 = 1;
+            if (has1) init1 = 1;
+            mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+            mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+            if (++stage == C::NS) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+        if (!alive) break;
+        mma_commit_pair(mapa_shared(smem_u32(&acc_full[buf]), 0));
+        mma_commit_pair(mapa_shared(smem_u32(&acc_full[buf]), 1));
+      }
+      if (!alive && issued_any) {
+        mma_commit_pair(mapa_shared(smem_u32(drain), 0));
+        const uint32_t a = smem_u32(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const uint64_t pol_out = policy_evict_first();
+    int i = 0;
+    for (int u = pid; u < n_units; u += pairs, ++i) {
+      const int m = u / p.R, r = u % p.R;
+      const int buf = i & 1;
+      const uint32_t use = uint32_t(i >> 1);
+      const bool got = mbar_wait(&acc_full[buf], use & 1u, ctl);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int cw = p.counts[r];
+      const bool any0 = (cw >> 16) & 1, any1 = (cw >> 17) & 1;
+      const int64_t row = int64_t(m) * 256 + int64_t(rank) * kBM + q * 32 + lane;
+      const bool row_ok = row < p.T;
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * C::ACC_COLS);
+#pragma unroll 1
+      for (int j = 0; j < B / 32; ++j) {
+        if constexpr (GU) {
+          uint32_t g[32], v[32];
+          tmem_ld32(tbase + j * 32, g);
+          tmem_ld32(tbase + 128 + j * 32, v);
+          tmem_ld_wait();
+          uint32_t hp[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const float g0 = any0 ? __uint_as_float(g[2 * t]) : 0.f, g1 = any0 ? __uint_as_float(g[2 * t + 1]) : 0.f;
+            const float u0 = any1 ? __uint_as_float(v[2 * t]) : 0.f, u1 = any1 ? __uint_as_float(v[2 * t + 1]) : 0.f;
+            hp[t] = pack_bf16x2(silu_fast(g0) * u0, silu_fast(g1) * u1);
+          }
+          if (row_ok) {
+            const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
+            __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(p.out) + off;
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              st_global_v4_hint(hrow + t * 8, hp[4 * t], hp[4 * t + 1], hp[4 * t + 2], hp[4 * t + 3], pol_out);
+            if (p.gate_pre) {
+              __nv_bfloat16* grow = static_cast<__nv_bfloat16*>(p.gate_pre) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                uint32_t w[4];
+#pragma unroll
+                for (int z = 0; z < 4; ++z)
+                  w[z] = any0 ? pack_bf16x2(__uint_as_float(g[8 * t + 2 * z]), __uint_as_float(g[8 * t + 2 * z + 1])) : 0u;
+                st_global_v4(grow + t * 8, w[0], w[1], w[2], w[3]);
+              }
+            }
+            if (p.up_out) {
+              __nv_bfloat16* urow = static_cast<__nv_bfloat16*>(p.up_out) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                uint32_t w[4];
+#pragma unroll
+                for (int z = 0; z < 4; ++z)
+                  w[z] = any1 ? pack_bf16x2(__uint_as_float(v[8 * t + 2 * z]), __uint_as_float(v[8 * t + 2 * z + 1])) : 0u;
+                st_global_v4(urow + t * 8, w[0], w[1], w[2], w[3]);
+              }
+            }
+          }
+        } else {
+          uint32_t a[32];
+          tmem_ld32(tbase + j * 32, a);
+          tmem_ld_wait();
+          float f[32];
+#pragma unroll
+          for (int t = 0; t < 32; ++t) f[t] = any0 ? __uint_as_float(a[t]) : 0.f;
+          if (row_ok) {
+            const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
+            if (p.add_residual) {
+              const __nv_bfloat16* rrow = static_cast<const __nv_bfloat16*>(p.residual) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const uint4 rv = ld_global_v4(rrow + t * 8);
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                  const float2 x2 = unpack_bf16x2(rw[w]);
+                  f[8 * t + 2 * w] += x2.x;
+                  f[8 * t + 2 * w + 1] += x2.y;
+                }
+              }
+            }
+            if (p.out_f32) {
+              float* orow = static_cast<float*>(p.out) + off;
+#pragma unroll
+              for (int t = 0; t < 8; ++t)
+                st_global_v4_hint(orow + t * 4, __float_as_uint(f[4 * t]), __float_as_uint(f[4 * t + 1]),
+                                  __float_as_uint(f[4 * t + 2]), __float_as_uint(f[4 * t + 3]), pol_out);
+            } else {
+              __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + off;
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                st_global_v4_hint(orow + t * 8, pack_bf16x2(f[8 * t], f[8 * t + 1]), pack_bf16x2(f[8 * t + 2], f[8 * t + 3]),
+                                  pack_bf16x2(f[8 * t + 4], f[8 * t + 5]), pack_bf16x2(f[8 * t + 6], f[8 * t + 7]),
+                                  pol_out);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace pair
+
 // ------------------------------------------------------------------- host
 
 struct EllArgs {
@@ -389,9 +706,49 @@ static int check_ell(const BellEll& e, const char* name) {
 // Weight tensor map: values [R, K, B, B] viewed as 2-D [R*K*B rows, B cols].
 static int make_w_map(CUtensorMap* m, const BellEll& e) {
   const uint64_t rows = uint64_t(e.R) * uint64_t(e.K) * uint64_t(e.B);
-  if (e.layout == BELL_TILE_IN_OUT)
-    return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, 64, Swz::B128);
-  return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, e.B, Swz::B128);
+  // both layouts: boxes of 64 x 64 (128-byte rows); a [B_out, B_in] tile is
+  // fetched as B/64 boxes of 64 N-rows
+  return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, 64, Swz::B128);
+}
+
+static bool pair_enabled() {
+  static const bool on = [] {
+    const char* s = std::getenv("BELL_SINGLE_CTA");
+    return !(s && s[0] == '1');
+  }();
+  return on;
+}
+
+template <bool GU, bool W_MN>
+static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p0,
+                       cudaStream_t stream) {
+  using C = pair::PCfg<GU>;
+  auto kern = pair::bell_bf16_pair_kernel<GU, W_MN>;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), C::SMEM)) return rc;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  Bf16Params p = p0;
+  p.n_mtiles = int32_t((p.T + 255) / 256);
+  const int64_t units = int64_t(p.n_mtiles) * p.R;
+  if (units == 0) return BELL_OK;
+  // persistent grid: as many CTA pairs as can be resident at once
+  static int max_pairs[2][2] = {{0, 0}, {0, 0}};
+  int& mp = max_pairs[GU][W_MN];
+  if (mp == 0) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(unsigned(sms & ~1));
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = C::SMEM;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &lc) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;
+    }
+    mp = n < sms / 2 ? n : sms / 2;
+  }
+  const int64_t pairs = units < mp ? units : mp;
+  kern<<<int(2 * pairs), kThreads, C::SMEM, stream>>>(a, w0, w1, p);
+  return check_launch(GU ? "bell gate/up pair kernel" : "bell linear pair kernel");
 }
 
 template <int B, bool GU, bool W_MN>
@@ -414,6 +771,7 @@ static int dispatch_bf16(int B, int layout, const CUtensorMap& a, const CUtensor
                          const Bf16Params& p, cudaStream_t s) {
   const bool mn = layout == BELL_TILE_IN_OUT;
   if (B == 64) return mn ? launch_bf16<64, GU, true>(a, w0, w1, p, s) : launch_bf16<64, GU, false>(a, w0, w1, p, s);
+  if (pair_enabled()) return mn ? launch_pair<GU, true>(a, w0, w1, p, s) : launch_pair<GU, false>(a, w0, w1, p, s);
   return mn ? launch_bf16<128, GU, true>(a, w0, w1, p, s) : launch_bf16<128, GU, false>(a, w0, w1, p, s);
 }
 

@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(128) bell_plan_kernel(PlanArgs a) {
     const int32_t* cu = a.ci_u + size_t(r) * a.K_u;
     uint32_t* out = a.gu_entries + size_t(r) * (a.K_g + a.K_u);
     uint32_t used[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint32_t gmatched[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     int n = 0, gany = 0, uany = 0, bad = 0;
     for (int k = 0; k < a.K_g; ++k) {
       const int c = cg[k];
@@ -207,18 +208,22 @@ __global__ void __launch_bounds__(128) bell_plan_kernel(PlanArgs a) {
         bad = 1;
         continue;
       }
-      uint32_t m = 255;
       for (int j = 0; j < a.K_u && a.merge; ++j) {
         if ((used[j >> 5] >> (j & 31)) & 1u) continue;
-        if (cu[j] == c) {
-          m = j;
+        if (cu[j] == c) {  // shared step: listed first (the 2-SM kernel relies on that order)
           used[j >> 5] |= 1u << (j & 31);
+          gmatched[k >> 5] |= 1u << (k & 31);
+          out[n++] = uint32_t(c) | (uint32_t(k) << 16) | (uint32_t(j) << 24);
+          gany = uany = 1;
           break;
         }
       }
-      out[n++] = uint32_t(c) | (uint32_t(k) << 16) | (m << 24);
+    }
+    for (int k = 0; k < a.K_g; ++k) {  // gate slots without an up partner, ascending
+      const int c = cg[k];
+      if (c < 0 || c >= a.C_gu || ((gmatched[k >> 5] >> (k & 31)) & 1u)) continue;
+      out[n++] = uint32_t(c) | (uint32_t(k) << 16) | (255u << 24);
       gany = 1;
-      if (m != 255) uany = 1;
     }
     for (int j = 0; j < a.K_u; ++j) {
       if ((used[j >> 5] >> (j & 31)) & 1u) continue;
