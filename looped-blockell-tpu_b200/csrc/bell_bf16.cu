@@ -59,9 +59,24 @@ struct Bf16Params {
   const void* residual;  // linear optional (bf16, same shape as out)
   int32_t add_residual;
   int32_t out_f32;   // linear: write fp32 instead of bf16
+  int32_t band;      // block-rows per band of the unit order (see unit_mr)
   int32_t* status;
   uint64_t timeout_ns;
 };
+
+// Work-unit order: bands of `band` output block-rows; inside a band, all
+// token tiles, block-row fastest.  Consecutive units share a token tile (its
+// activation panel stays in L2) and a band's weight tiles stay L2-resident
+// while every token tile passes, instead of the whole weight set cycling
+// through L2 once per token tile.
+__device__ __forceinline__ void unit_mr(int u, const Bf16Params& p, int& m, int& r) {
+  const int per_band = p.n_mtiles * p.band;
+  const int b = u / per_band;
+  const int rem = u - b * per_band;
+  const int rows = min(p.band, p.R - b * p.band);
+  m = rem / rows;
+  r = b * p.band + (rem - m * rows);
+}
 
 // Load one [64 K x B] weight chunk of tile `tile` (global tile index r*K+k).
 template <int B, bool W_MN>
@@ -141,7 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool alive = true;
       for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
-        const int m = u / p.R, r = u % p.R;
+        int m, r;
+        unit_mr(u, p, m, r);
         const int n = p.counts[r] & 0xFFFF;
         const uint32_t* plan = p.plan + size_t(r) * p.S;
         for (int s = 0; s < n && alive; ++s) {
@@ -197,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool issued_any = false;
       int i = 0;
       for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x, ++i) {
-        const int r = u % p.R;
+        int m_unused, r;
+        unit_mr(u, p, m_unused, r);
         const int buf = i & 1;
         const uint32_t use = uint32_t(i >> 1);
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
@@ -258,7 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     int i = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
-      const int m = u / p.R, r = u % p.R;
+      int m, r;
+        unit_mr(u, p, m, r);
       const int buf = i & 1;
       const uint32_t use = uint32_t(i >> 1);
       const bool got = mbar_wait(&acc_full[buf], use & 1u, ctl);
@@ -389,7 +407,7 @@ static constexpr int W_BYTES = kBK * 128 * 2;  // 16 KB: one [64 K x 128 N] box 
 template <bool GU>
 struct PCfg {
   static constexpr int STAGE = A_BYTES + W_BYTES;  // 32 KB (linear steps use half of W)
-  static constexpr int NS = 6;
+  static constexpr int NS = 7;
   static constexpr int ACC_COLS = GU ? 256 : 128;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;
   static constexpr int SMEM = NS * STAGE + 1024 + 512;
@@ -447,7 +465,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool alive = true;
       for (int u = pid; u < n_units && alive; u += pairs) {
-        const int m = u / p.R, r = u % p.R;
+        int m, r;
+        unit_mr(u, p, m, r);
         const int n = p.counts[r] & 0xFFFF;
         const uint32_t* plan = p.plan + size_t(r) * p.S;
         for (int s = 0; s < n && alive; ++s) {
@@ -507,7 +526,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool alive = true, issued_any = false;
       for (int u = pid; u < n_units && alive; u += pairs, ++i) {
-        const int r = u % p.R;
+        int m_unused, r;
+        unit_mr(u, p, m_unused, r);
         const int buf = i & 1;
         const uint32_t use = uint32_t(i >> 1);
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
@@ -573,7 +593,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint64_t pol_out = policy_evict_first();
     int i = 0;
     for (int u = pid; u < n_units; u += pairs, ++i) {
-      const int m = u / p.R, r = u % p.R;
+      int m, r;
+        unit_mr(u, p, m, r);
       const int buf = i & 1;
       const uint32_t use = uint32_t(i >> 1);
       const bool got = mbar_wait(&acc_full[buf], use & 1u, ctl);
@@ -711,6 +732,8 @@ static int make_w_map(CUtensorMap* m, const BellEll& e) {
   return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, 64, Swz::B128);
 }
 
+static int unit_band(bool gate_up, int R);
+
 static bool pair_enabled() {
   static const bool on = [] {
     const char* s = std::getenv("BELL_SINGLE_CTA");
@@ -729,6 +752,7 @@ static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   if (int rc = device_sm_count(&sms)) return rc;
   Bf16Params p = p0;
   p.n_mtiles = int32_t((p.T + 255) / 256);
+  p.band = unit_band(GU, p.R);
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
   // persistent grid: as many CTA pairs as can be resident at once
@@ -751,10 +775,24 @@ static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   return check_launch(GU ? "bell gate/up pair kernel" : "bell linear pair kernel");
 }
 
+// Rows per band of the unit order: gate/up bands of 32 block-rows keep
+// 32 x (K_g + K_u) weight tiles hot in L2 while all token tiles pass; the down
+// projection's whole weight set is small enough to stay resident unbanded.
+static int unit_band(bool gate_up, int R) {
+  static const int env = [] {
+    const char* s = std::getenv("BELL_BAND_ROWS");
+    return s ? std::atoi(s) : 0;
+  }();
+  int band = gate_up ? (env > 0 ? env : 32) : R;
+  return band < 1 ? 1 : (band > R ? R : band);
+}
+
 template <int B, bool GU, bool W_MN>
-static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p,
+static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p0,
                        cudaStream_t stream) {
   using C = Cfg<B, GU>;
+  Bf16Params p = p0;
+  p.band = unit_band(GU, p.R);
   auto kern = bell_bf16_kernel<B, GU, W_MN>;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
   int sms = 0;
