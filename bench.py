@@ -140,6 +140,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=5)
     ap.add_argument("--shared-gate-up", action="store_true")
+    ap.add_argument("--layout", default="in_out", choices=["in_out", "out_in"], help="weight tile layout")
     ap.add_argument("--tokens", type=int, default=0, help="override T (profiling on a smaller case)")
     ap.add_argument("--ref-tokens", type=int, default=2048)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
@@ -177,6 +178,10 @@ def run_gpu(args, cfg, rank, world):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
     c = make_ffn(cfg, device="cuda", shared_gate_up=args.shared_gate_up)
+    lay = ops.TILE_OUT_IN if args.layout == "out_in" else ops.TILE_IN_OUT
+    if lay == ops.TILE_OUT_IN:  # same weights, stored [B_out, B_in]
+        for k in ("vg", "vu", "vd"):
+            c[k] = c[k].transpose(-1, -2).contiguous()
     T, d, F = cfg.T, cfg.d_model, cfg.d_ff
     launches_per_step = 3
     if world > 1:
@@ -192,8 +197,8 @@ def run_gpu(args, cfg, rank, world):
         h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
 
         def step(x):
-            return ops._swiglu(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], True, ops.TILE_IN_OUT, False,
-                               out=out, h=h)[0]
+            return ops._swiglu(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], True, lay, False,
+                               out=out, h=h, shared_topology=args.shared_gate_up)[0]
 
     x = c["x"]
     for _ in range(args.warmup):
@@ -233,9 +238,11 @@ def run_gpu(args, cfg, rank, world):
         desc.T, desc.d_model, desc.d_ff, desc.dtype, desc.add_residual = T, d, F, 0, 1
         desc.x, desc.h, desc.out, desc.plan = x.data_ptr(), h.data_ptr(), out.data_ptr(), plan.data_ptr()
         B = cfg.B
-        desc.gate = ops._ell(c["vg"], c["cg"], d // B, 0)
-        desc.up = ops._ell(c["vu"], c["cu"], d // B, 0)
-        desc.down = ops._ell(c["vd"], c["cd"], F // B, 0)
+        desc.gate = ops._ell(c["vg"], c["cg"], d // B, lay)
+        if args.shared_gate_up:
+            desc.gate.flags = _lib.BELL_ELL_SAME_COLS_AS_UP
+        desc.up = ops._ell(c["vu"], c["cu"], d // B, lay)
+        desc.down = ops._ell(c["vd"], c["cd"], F // B, lay)
         s = ops._stream()
         for _ in range(2):
             _lib.check(lib.bell_gate_up_bf16(C.byref(desc), s), "gate_up")
@@ -285,7 +292,7 @@ def run_gpu(args, cfg, rank, world):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": cfg.name, "T": T, "d_model": d, "d_ff": F, "B": cfg.B, "density": cfg.density,
-                       "gate_up_topology": "shared" if args.shared_gate_up else "independent",
+                       "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
                        "parallelism": f"dff{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (x is 2 GiB)"},
             "tflops_effective": tflops, "tflops_effective_per_gpu": tflops / world,

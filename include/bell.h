@@ -64,8 +64,14 @@ typedef struct BellEll {
   const int32_t* col_indices;  /* [R, K]                                    */
   int32_t R, C, K, B;          /* block-rows, block-cols, slots/row, tile   */
   int32_t layout;              /* BELL_TILE_IN_OUT / BELL_TILE_OUT_IN        */
-  int32_t reserved;
+  int32_t flags;               /* BELL_ELL_* hints (0 = none)                 */
 } BellEll;
+
+/* BellFFNDesc.gate.flags: the gate and up col_indices hold the same columns
+ * (the reference MLPBlock's default, looped_blockell/layers/mlp.py:84-95).
+ * Identical col_indices pointers imply it.  The forward then loads each
+ * activation tile once for both projections. */
+#define BELL_ELL_SAME_COLS_AS_UP 1
 
 /*
  * SwiGLU feed-forward: out = W_down(silu(W_gate x) * W_up x) (+ residual).

@@ -22,15 +22,11 @@
 // overlaps the MMAs of unit i+1.  Every wait is bounded (bell_ptx.cuh).
 #include <string>
 
+#include "bell_bf16.cuh"
 #include "bell_host.h"
 #include "bell_ptx.cuh"
 
 namespace bell {
-
-static constexpr int kBM = 128;        // tokens per tile (MMA M)
-static constexpr int kBK = 64;         // K elements per pipeline stage (128 B of bf16)
-static constexpr int kThreads = 192;   // 6 warps
-static constexpr uint32_t kNone = 255;
 
 template <int B, bool GU>
 struct Cfg {
@@ -44,39 +40,6 @@ struct Cfg {
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
 };
 
-struct Bf16Params {
-  int64_t T;
-  int32_t n_mtiles;
-  int32_t R;         // output block-rows
-  int32_t K0, K1;    // slots per row of w0 / w1
-  int32_t S;         // plan entries per row
-  const uint32_t* plan;
-  const int32_t* counts;
-  void* out;         // GU: h [T, R*B] bf16; linear: out [T, R*B]
-  int64_t ld_out;    // elements
-  void* gate_pre;    // GU optional
-  void* up_out;      // GU optional
-  const void* residual;  // linear optional (bf16, same shape as out)
-  int32_t add_residual;
-  int32_t out_f32;   // linear: write fp32 instead of bf16
-  int32_t band;      // block-rows per band of the unit order (see unit_mr)
-  int32_t* status;
-  uint64_t timeout_ns;
-};
-
-// Work-unit order: bands of `band` output block-rows; inside a band, all
-// token tiles, block-row fastest.  Consecutive units share a token tile (its
-// activation panel stays in L2) and a band's weight tiles stay L2-resident
-// while every token tile passes, instead of the whole weight set cycling
-// through L2 once per token tile.
-__device__ __forceinline__ void unit_mr(int u, const Bf16Params& p, int& m, int& r) {
-  const int per_band = p.n_mtiles * p.band;
-  const int b = u / per_band;
-  const int rem = u - b * per_band;
-  const int rows = min(p.band, p.R - b * p.band);
-  m = rem / rows;
-  r = b * p.band + (rem - m * rows);
-}
 
 // Load one [64 K x B] weight chunk of tile `tile` (global tile index r*K+k).
 template <int B, bool W_MN>
@@ -206,6 +169,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // --------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_1 = idesc_bf16(kBM, B, false, W_MN);
+      constexpr uint64_t kBStep = W_MN ? (2048 >> 4) : (32 >> 4);
+      const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(smem) + C::A_BYTES, 8192, 1024)
+                                    : sdesc_sw128(smem_u32(smem) + C::A_BYTES, 16, 1024);
       constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
       int stage = 0;
       uint32_t phase = 0;
@@ -234,18 +201,25 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
-            const uint32_t w0_addr = a_addr + C::A_BYTES;
-            const uint32_t w1_addr = w0_addr + C::W_BYTES;
+            // stage descriptors = stage-0 descriptors + constant start-address offsets
+            const uint64_t ad = a_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
+            const uint64_t bd0 = b_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
+            const uint64_t bd1 = bd0 + (C::W_BYTES >> 4);
             const bool fused = GU && has0 && has1 && (init0 == init1);
+            if (fused) {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t adesc = sdesc_sw128(a_addr + kk * 32, 16, 1024);
-              if (fused) {
-                mma_bf16(d0, adesc, w_desc<B, W_MN>(w0_addr, kk), IDESC_2, (kk > 0) ? 1u : init0);
-              } else {
-                if (has0) mma_bf16(d0, adesc, w_desc<B, W_MN>(w0_addr, kk), IDESC_1, (kk > 0) ? 1u : init0);
-                if (has1) mma_bf16(d1, adesc, w_desc<B, W_MN>(w1_addr, kk), IDESC_1, (kk > 0) ? 1u : init1);
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_2, kk > 0 ? 1u : init0);
+            } else {
+              if (has0) {
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                  mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init0);
+              }
+              if (has1) {
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                  mma_bf16(d1, ad + 2 * kk, bd1 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init1);
               }
             }
             issued_any = true;
@@ -522,6 +496,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0 && rank == 0) {  // --------------------- MMA issuer (even CTA)
       constexpr uint32_t IDESC_N128 = idesc_bf16(256, 128, false, W_MN);
       constexpr uint32_t IDESC_N256 = idesc_bf16(256, 256, false, W_MN);
+      // K step of 16 elements: +32 B inside a K-major row, +16 rows (2048 B) for MN-major B
+      constexpr uint64_t kBStep = W_MN ? (2048 >> 4) : (32 >> 4);
+      const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(smem) + A_BYTES, 8192, 1024)
+                                    : sdesc_sw128(smem_u32(smem) + A_BYTES, 16, 1024);
+      const uint32_t empty_c0 = mapa_shared(smem_u32(&empty[0]), 0);
+      const uint32_t empty_c1 = mapa_shared(smem_u32(&empty[0]), 1);
       int stage = 0, i = 0;
       uint32_t phase = 0;
       bool alive = true, issued_any = false;
@@ -547,28 +528,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a_addr = smem_u32(smem + stage * C::STAGE);
-            const uint32_t w_addr = a_addr + A_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t adesc = sdesc_sw128(a_addr + kk * 32, 16, 1024);
-              const uint64_t bdesc = W_MN ? sdesc_sw128(w_addr + kk * 2048, 8192, 1024)
-                                          : sdesc_sw128(w_addr + kk * 32, 16, 1024);
-              if (fused) {
-                // The plan lists a row's shared steps before its single ones, so gate and
-                // up are always in the same state here (one N=256 MMA spans both CTAs'
-                // halves and cannot initialise one accumulator and add to the other).
-                mma_bf16_pair(d0, adesc, bdesc, IDESC_N256, kk > 0 ? 1u : init0);
-                if (kk == 0 && init0 != init1) atomicOr(p.status, BELL_STATUS_INTERNAL);
-              } else {
-                mma_bf16_pair(has0 ? d0 : d1, adesc, bdesc, IDESC_N128, kk > 0 ? 1u : (has0 ? init0 : init1));
-              }
+            // Straight-line issue: descriptors are the stage-0 descriptors plus
+            // constant offsets in their 16-byte start-address field.
+            const uint64_t ad = a_desc0 + uint64_t(stage) * (C::STAGE >> 4);
+            const uint64_t bd = b_desc0 + uint64_t(stage) * (C::STAGE >> 4);
+            if (fused) {
+              // The plan lists a row's shared steps before its single ones, so gate and
+              // up are always in the same state here (one N=256 MMA spans both CTAs'
+              // halves and cannot initialise one accumulator and add to the other).
+              mma_bf16_pair(d0, ad, bd, IDESC_N256, init0);
+              mma_bf16_pair(d0, ad + 2, bd + kBStep, IDESC_N256, 1u);
+              mma_bf16_pair(d0, ad + 4, bd + 2 * kBStep, IDESC_N256, 1u);
+              mma_bf16_pair(d0, ad + 6, bd + 3 * kBStep, IDESC_N256, 1u);
+              if (init0 != init1) atomicOr(p.status, BELL_STATUS_INTERNAL);
+            } else {
+              const uint32_t dd = has0 ? d0 : d1;
+              mma_bf16_pair(dd, ad, bd, IDESC_N128, has0 ? init0 : init1);
+              mma_bf16_pair(dd, ad + 2, bd + kBStep, IDESC_N128, 1u);
+              mma_bf16_pair(dd, ad + 4, bd + 2 * kBStep, IDESC_N128, 1u);
+              mma_bf16_pair(dd, ad + 6, bd + 3 * kBStep, IDESC_N128, 1u);
             }
             issued_any = true;
             if (has0) init0 = 1;
             if (has1) init1 = 1;
-            mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
-            mma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+            mma_commit_pair(empty_c0 + uint32_t(stage) * 8u);
+            mma_commit_pair(empty_c1 + uint32_t(stage) * 8u);
             if (++stage == C::NS) {
               stage = 0;
               phase ^= 1;
@@ -734,13 +718,24 @@ static int make_w_map(CUtensorMap* m, const BellEll& e) {
 
 static int unit_band(bool gate_up, int R);
 
-static bool pair_enabled() {
-  static const bool on = [] {
-    const char* s = std::getenv("BELL_SINGLE_CTA");
-    return !(s && s[0] == '1');
+// B = 128 kernel family: 0 feature-major (default), 1 CTA-pair token-major,
+// 2 single-CTA token-major (BELL_BF16_KERNEL=fmajor|pair|single).
+static int b128_kernel() {
+  static const int k = [] {
+    const char* s = std::getenv("BELL_BF16_KERNEL");
+    if (s && std::string(s) == "pair") return 1;
+    if (s && std::string(s) == "single") return 2;
+    const char* old = std::getenv("BELL_SINGLE_CTA");
+    if (old && old[0] == '1') return 2;
+    return 0;
   }();
-  return on;
+  return k;
 }
+
+static bool pair_enabled() { return b128_kernel() == 1; }
+
+// Rows of the activation TMA box: the feature-major kernels take 256 tokens.
+static uint32_t a_box_rows(int B) { return (B == 128 && b128_kernel() == 0) ? 256u : uint32_t(kBM); }
 
 template <bool GU, bool W_MN>
 static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p0,
@@ -809,8 +804,40 @@ static int dispatch_bf16(int B, int layout, const CUtensorMap& a, const CUtensor
                          const Bf16Params& p, cudaStream_t s) {
   const bool mn = layout == BELL_TILE_IN_OUT;
   if (B == 64) return mn ? launch_bf16<64, GU, true>(a, w0, w1, p, s) : launch_bf16<64, GU, false>(a, w0, w1, p, s);
+  if (b128_kernel() == 0) {
+    Bf16Params q = p;
+    q.band = unit_band(GU, p.R);
+    if (!GU && p.add_residual) {  // the feature-major linear reads the residual with TMA
+      CUtensorMap mr;
+      if (int rc = make_map_2d(&mr, p.residual, MapType::BF16, uint64_t(p.ld_out), uint64_t(p.T),
+                               uint64_t(p.ld_out) * 2, 64, 256, Swz::B128))
+        return rc;
+      return launch_fmajor(GU, mn, a, w0, mr, q, s);
+    }
+    return launch_fmajor(GU, mn, a, w0, w1, q, s);
+  }
   if (pair_enabled()) return mn ? launch_pair<GU, true>(a, w0, w1, p, s) : launch_pair<GU, false>(a, w0, w1, p, s);
   return mn ? launch_bf16<128, GU, true>(a, w0, w1, p, s) : launch_bf16<128, GU, false>(a, w0, w1, p, s);
+}
+
+// Tile-schedule plan of one bf16 SwiGLU forward.  Gate/up slots on the same
+// column share a step unless the B = 128 gate/up kernel runs one weight tile
+// per step (feature-major split mode).
+// Split mode (one weight tile per gate/up step, 48-KB stages, 4 deep) suits
+// independent gate/up topologies; fused steps (x loaded once for both
+// projections) suit shared ones.
+static bool use_split(const BellFFNDesc* d) {
+  if (d->gate.B != 128 || b128_kernel() != 0) return false;
+  const int env = fmajor_split_env();
+  if (env >= 0) return env == 1;
+  const bool same = (d->gate.flags & BELL_ELL_SAME_COLS_AS_UP) || d->gate.col_indices == d->up.col_indices;
+  return !same;
+}
+
+int launch_ffn_plan(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
+  const int merge = use_split(d) ? 0 : 1;
+  return launch_plan_ex(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
+                        d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s, merge);
 }
 
 int check_ffn(const BellFFNDesc* d, int dtype) {
@@ -844,7 +871,8 @@ int check_ffn(const BellFFNDesc* d, int dtype) {
 int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   const BellEll &g = d->gate, &u = d->up;
   CUtensorMap ma, mg, mu;
-  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64, kBM, Swz::B128))
+  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64, a_box_rows(g.B),
+                           Swz::B128))
     return rc;
   if (int rc = make_w_map(&mg, g)) return rc;
   if (int rc = make_w_map(&mu, u)) return rc;
@@ -864,13 +892,15 @@ int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.up_out = d->up_out;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
+  p.split = use_split(d) ? 1 : 0;  // must match the plan built by launch_ffn_plan
   return dispatch_bf16<true>(g.B, g.layout, ma, mg, mu, p, s);
 }
 
 int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   const BellEll& w = d->down;
   CUtensorMap ma, mw;
-  if (int rc = make_map_2d(&ma, d->h, MapType::BF16, d->d_ff, d->T, uint64_t(d->d_ff) * 2, 64, kBM, Swz::B128))
+  if (int rc = make_map_2d(&ma, d->h, MapType::BF16, d->d_ff, d->T, uint64_t(d->d_ff) * 2, 64, a_box_rows(w.B),
+                           Swz::B128))
     return rc;
   if (int rc = make_w_map(&mw, w)) return rc;
   PlanLayout L = plan_layout(d->gate.R, d->gate.K, d->up.K, w.R, w.K);
@@ -906,9 +936,7 @@ int bell_swiglu_fwd_bf16(const BellFFNDesc* d, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int32_t* status = d->status ? d->status : default_status_ptr();
   if (!status) return BELL_ERR_LAUNCH;
-  if (int rc = launch_plan(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
-                           d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s))
-    return rc;
+  if (int rc = launch_ffn_plan(d, status, s)) return rc;
   if (int rc = gate_up_bf16(d, status, s)) return rc;
   return down_bf16(d, status, s);
 }
@@ -920,9 +948,7 @@ int bell_gate_up_bf16(const BellFFNDesc* d, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int32_t* status = d->status ? d->status : default_status_ptr();
   if (!status) return BELL_ERR_LAUNCH;
-  if (int rc = launch_plan(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
-                           d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s))
-    return rc;
+  if (int rc = launch_ffn_plan(d, status, s)) return rc;
   return gate_up_bf16(d, status, s);
 }
 
@@ -946,7 +972,8 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   if (int rc = launch_plan(nullptr, 0, nullptr, 0, 0, 0, w.col_indices, w.K, w.R, w.C, d->plan, status, s)) return rc;
   const int64_t in_f = int64_t(w.C) * w.B, out_f = int64_t(w.R) * w.B;
   CUtensorMap ma, mw;
-  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, in_f, d->T, uint64_t(in_f) * 2, 64, kBM, Swz::B128)) return rc;
+  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, in_f, d->T, uint64_t(in_f) * 2, 64, a_box_rows(w.B), Swz::B128))
+    return rc;
   if (int rc = make_w_map(&mw, w)) return rc;
   PlanLayout L = plan_layout(0, 0, 0, w.R, w.K);
   Bf16Params p{};

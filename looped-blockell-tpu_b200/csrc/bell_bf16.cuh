@@ -1,0 +1,60 @@
+// bell_bf16.cuh — definitions shared by the bf16 Block-ELL kernels
+// (bell_bf16.cu: token-major kernels; bell_bf16_t.cu: feature-major kernels).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace bell {
+
+static constexpr int kBM = 128;        // tokens per tile (MMA M) in the token-major kernels
+static constexpr int kBK = 64;         // K elements per pipeline stage (128 B of bf16)
+static constexpr int kThreads = 192;   // 6 warps
+static constexpr uint32_t kNone = 255;
+
+struct Bf16Params {
+  int64_t T;
+  int32_t n_mtiles;
+  int32_t R;         // output block-rows
+  int32_t K0, K1;    // slots per row of w0 / w1
+  int32_t S;         // plan entries per row
+  const uint32_t* plan;
+  const int32_t* counts;
+  void* out;         // GU: h [T, R*B] bf16; linear: out [T, R*B]
+  int64_t ld_out;    // elements
+  void* gate_pre;    // GU optional
+  void* up_out;      // GU optional
+  const void* residual;  // linear optional (bf16, same shape as out)
+  int32_t add_residual;
+  int32_t out_f32;   // linear: write fp32 instead of bf16
+  int32_t band;      // block-rows per band of the unit order (see unit_mr)
+  int32_t split;     // feature-major gate/up: one weight tile per plan step
+  int32_t* status;
+  uint64_t timeout_ns;
+};
+
+// Work-unit order: bands of `band` output block-rows; inside a band, all
+// token tiles, block-row fastest.  Consecutive units share a token tile (its
+// activation panel stays in L2) and a band's weight tiles stay L2-resident
+// while every token tile passes, instead of the whole weight set cycling
+// through L2 once per token tile.
+__device__ __forceinline__ void unit_mr(int u, const Bf16Params& p, int& m, int& r) {
+  const int per_band = p.n_mtiles * p.band;
+  const int b = u / per_band;
+  const int rem = u - b * per_band;
+  const int rows = min(p.band, p.R - b * p.band);
+  m = rem / rows;
+  r = b * p.band + (rem - m * rows);
+}
+
+// Feature-major (transposed) B = 128 kernels, bell_bf16_t.cu.  `a` is the
+// activation map with 256-row boxes.
+// BELL_GU_SPLIT override for the feature-major gate/up kernel: -1 automatic,
+// 0 fused steps, 1 one weight tile per step (plan built without merging)
+int fmajor_split_env();
+int launch_fmajor(bool gate_up, bool w_mn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
+                  const Bf16Params& p, cudaStream_t stream);
+
+}  // namespace bell

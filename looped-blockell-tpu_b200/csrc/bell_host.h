@@ -59,6 +59,7 @@ int launch_plan_ex(const int32_t* ci_g, int32_t K_g, const int32_t* ci_u, int32_
 // bf16 building blocks (bell_bf16.cu): descriptor checks, the gate/up launch
 // and the down (linear + residual) launch, on an already-built plan.
 int check_ffn(const BellFFNDesc* d, int dtype);
+int launch_ffn_plan(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
 int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
 int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
 

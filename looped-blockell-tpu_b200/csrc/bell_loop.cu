@@ -140,9 +140,7 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   if (d->T == 0 || d->L == 0) return BELL_OK;
   int32_t* status = d->status ? d->status : default_status_ptr();
   if (!status) return BELL_ERR_LAUNCH;
-  if (int rc = launch_plan(d->gate.col_indices, d->gate.K, d->up.col_indices, d->up.K, d->gate.R, d->gate.C,
-                           d->down.col_indices, d->down.K, d->down.R, d->down.C, d->plan, status, s))
-    return rc;
+  if (int rc = launch_ffn_plan(&f, status, s)) return rc;
   for (int it = 0; it < d->L; ++it) {
     if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
     if (int rc = gate_up_bf16(&f, status, s)) return rc;

@@ -26,7 +26,10 @@ ERRORS = {-1: "DTYPE", -2: "SHAPE", -3: "ALIGN", -4: "ARCH", -5: "LAUNCH", -6: "
 
 class BellEll(C.Structure):
     _fields_ = [("values", C.c_void_p), ("col_indices", C.c_void_p), ("R", C.c_int32), ("C", C.c_int32),
-                ("K", C.c_int32), ("B", C.c_int32), ("layout", C.c_int32), ("reserved", C.c_int32)]
+                ("K", C.c_int32), ("B", C.c_int32), ("layout", C.c_int32), ("flags", C.c_int32)]
+
+
+BELL_ELL_SAME_COLS_AS_UP = 1
 
 
 class BellFFNDesc(C.Structure):

@@ -63,7 +63,7 @@ def plan_bytes(R_gu: int, K_g: int, K_u: int, R_d: int, K_d: int) -> int:
 
 
 def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, want_intermediates,
-            residual=None, out=None, h=None):
+            residual=None, out=None, h=None, shared_topology=False):
     lib = _lib.load()
     _check_cuda("x", x)
     if x.dim() != 2:
@@ -100,6 +100,8 @@ def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layo
     desc.up_out = up_out.data_ptr() if up_out is not None else None
     desc.out, desc.plan = out.data_ptr(), plan.data_ptr()
     desc.gate = _ell(vg, cg, d_model // B, layout)
+    if shared_topology:
+        desc.gate.flags = _lib.BELL_ELL_SAME_COLS_AS_UP
     desc.up = _ell(vu, cu, d_model // B, layout)
     desc.down = _ell(vd, cd, d_ff // vd.shape[2], layout)
     desc.status = None
@@ -138,15 +140,22 @@ def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: 
 
 
 def block_ell_swiglu_fwd(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual: bool = False,
-                         layout: int = TILE_IN_OUT) -> torch.Tensor:
-    """``W_down(silu(W_gate x) * W_up x) (+ x)`` — reference titan::block_ell_swiglu_fwd."""
-    return _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, False)[0]
+                         layout: int = TILE_IN_OUT, shared_topology: bool = False) -> torch.Tensor:
+    """``W_down(silu(W_gate x) * W_up x) (+ x)`` — reference titan::block_ell_swiglu_fwd.
+
+    ``shared_topology=True`` tells the kernel that gate and up hold the same
+    column lists (the reference MLPBlock's default); results are identical
+    either way, only the schedule changes."""
+    return _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, False,
+                   shared_topology=shared_topology)[0]
 
 
 def block_ell_swiglu_fwd_with_intermediate(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down,
-                                           add_residual: bool = False, layout: int = TILE_IN_OUT):
+                                           add_residual: bool = False, layout: int = TILE_IN_OUT,
+                                           shared_topology: bool = False):
     """Returns (result, h, gate_pre_act, up_output) like the reference op (block_ell_ops.cpp:65-76)."""
-    return _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, True)
+    return _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, True,
+                   shared_topology=shared_topology)
 
 
 def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, residual: Optional[torch.Tensor] = None,

@@ -88,6 +88,9 @@ class MLPBlock(nn.Module):
             self.w_gate = BlockELLLinear(d_ff, d_model, bias=False, **kw)
             self.w_up = BlockELLLinear(d_ff, d_model, bias=False, **kw)
             self.w_down = BlockELLLinear(d_model, d_ff, bias=False, **kw)
+            # gate and up are seeded alike, so their topologies start identical (reference
+            # mlp.py:84-95); code that edits one topology should clear this hint
+            self.gate_up_shared = bool(torch.equal(self.w_gate.col_indices, self.w_up.col_indices))
         else:
             self.fc1 = BlockELLLinear(d_ff, d_model, **kw)
             self.fc2 = BlockELLLinear(d_model, d_ff, **kw)
@@ -100,7 +103,7 @@ class MLPBlock(nn.Module):
             out = block_ell_swiglu_fwd(x2, self.w_gate.kernel_values(), self.w_gate.effective_col_indices(),
                                        self.w_up.kernel_values(), self.w_up.effective_col_indices(),
                                        self.w_down.kernel_values(), self.w_down.effective_col_indices(),
-                                       add_residual=residual)
+                                       add_residual=residual, shared_topology=self.gate_up_shared)
             out = out.reshape(*lead, self.d_model)
         else:
             out = self.fc2(F.gelu(self.fc1(x)))
