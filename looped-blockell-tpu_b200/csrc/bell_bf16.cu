@@ -25,6 +25,7 @@
 #include "bell_bf16.cuh"
 #include "bell_host.h"
 #include "bell_ptx.cuh"
+#include "bell_sched.cuh"
 
 namespace bell {
 
@@ -36,10 +37,16 @@ struct Cfg {
   static constexpr int NS = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
   static constexpr int ACC_COLS = GU ? 2 * B : B;       // fp32 columns per accumulator buffer
   static constexpr int TMEM_COLS = 2 * ACC_COLS;        // double buffered
-  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+  // align + barriers (512) + stage info (64) + two staged plan rows
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + 2 * kRowMax * 4;
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
 };
 
+
+// Single-CTA token-major kernel: warp 0 and warp 6 TMA producers, warp 1
+// TMEM owner + MMA issuer, warps 2-5 epilogue.
+static constexpr int kTmThreads = 224;
+static constexpr int kTmProd1 = 6;
 
 // Load one [64 K x B] weight chunk of tile `tile` (global tile index r*K+k).
 template <int B, bool W_MN>
@@ -64,19 +71,22 @@ __device__ __forceinline__ uint64_t w_desc(uint32_t w_addr, int kk) {
 }
 
 template <int B, bool GU, bool W_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kTmThreads, 1)
     bell_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w0,
                      const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
   using C = Cfg<B, GU>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE_BYTES);
+  uint8_t* ctl_base = smem + C::NS * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctl_base);
   uint64_t* empty = full + C::NS;
   uint64_t* acc_full = empty + C::NS;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* stage_info = reinterpret_cast<uint32_t*>(ctl_base + 512);
+  uint32_t* rows = reinterpret_cast<uint32_t*>(ctl_base + 576);  // one plan row per producer warp
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -105,63 +115,98 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int n_units = p.n_mtiles * p.R;
+  constexpr int KC = B / kBK;  // stages per plan step
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
+  if (warp == 0 || warp == kTmProd1) {
+    // ----------------------------------------------------------- producers
+    // Two producer warps take alternate stage uses (use g goes to warp g & 1).
+    // Each warp stages its plan rows through shared memory one unit ahead;
+    // lane 0 issues the copies and writes each stage's info word.
+    const int pid = warp == 0 ? 0 : 1;
+    uint32_t* row = rows + pid * kRowMax;
+    if (pid == 0 && lane == 0) {
       prefetch_tmap(&tm_a);
       prefetch_tmap(&tm_w0);
       if (GU) prefetch_tmap(&tm_w1);
-      const uint64_t pol_a = policy_evict_normal();
-      const uint64_t pol_w = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      bool alive = true;
-      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
-        int m, r;
-        unit_mr(u, p, m, r);
-        const int n = p.counts[r] & 0xFFFF;
-        const uint32_t* plan = p.plan + size_t(r) * p.S;
-        for (int s = 0; s < n && alive; ++s) {
-          const uint32_t e = plan[s];
-          const int c = int(e & 0xFFFFu);
-          const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
-          const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
-          const uint32_t bytes = C::A_BYTES + (has0 ? C::W_BYTES : 0) + (has1 ? C::W_BYTES : 0);
-          for (int kc = 0; kc < B / kBK; ++kc) {
+    }
+    const uint64_t pol_a = policy_evict_normal();
+    const uint64_t pol_w = policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0, g = 0;
+    int last_stage = -1;
+    uint32_t last_phase = 0;
+    bool alive = true;
+    RowAhead ahead;
+    if (blockIdx.x < n_units) {
+      int m0, r0;
+      unit_mr(blockIdx.x, p, m0, r0);
+      row_fetch(ahead, p.plan, p.counts, p.S, r0);
+    }
+    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+      int m, r;
+      unit_mr(u, p, m, r);
+      const int n = ahead.cnt & 0xFFFF;
+      row_put(ahead, row, p.S);
+      __syncwarp();
+      if (u + int(gridDim.x) < n_units) {
+        int m2, r2;
+        unit_mr(u + gridDim.x, p, m2, r2);
+        row_fetch(ahead, p.plan, p.counts, p.S, r2);
+      }
+      if (lane == 0) {
+        const int uses = n > 0 ? n * KC : 1;  // a unit without live steps: one empty stage
+        for (int j = 0; j < uses; ++j, ++g) {
+          if (int(g & 1u) == pid) {
             if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
               alive = false;
               break;
             }
-            uint8_t* st = smem + stage * C::STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[stage], bytes);
-            tma_load_2d(st, &tm_a, &full[stage], c * B + kc * kBK, m * kBM, pol_a);
-            if (has0) load_w_chunk<B, W_MN>(st + C::A_BYTES, &tm_w0, &full[stage], r * p.K0 + int(k0), kc, pol_w);
-            if (has1)
-              load_w_chunk<B, W_MN>(st + C::A_BYTES + C::W_BYTES, &tm_w1, &full[stage], r * p.K1 + int(k1), kc,
-                                    pol_w);
-            ++issued;
-            if (++stage == C::NS) {
-              stage = 0;
-              phase ^= 1;
+            uint32_t info = (j == 0 ? kSiFirst : 0u) | (j == uses - 1 ? kSiLast : 0u);
+            if (n > 0) {
+              const uint32_t e = row[j / KC];
+              const int kc = j % KC;
+              const int c = int(e & 0xFFFFu);
+              const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+              const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
+              info |= (has0 ? kSiHas0 : 0u) | (has1 ? kSiHas1 : 0u);
+              stage_info[stage] = info;
+              uint8_t* st = smem + stage * C::STAGE_BYTES;
+              mbar_arrive_expect_tx(&full[stage],
+                                    C::A_BYTES + (has0 ? C::W_BYTES : 0) + (has1 ? C::W_BYTES : 0));
+              tma_load_2d(st, &tm_a, &full[stage], c * B + kc * kBK, m * kBM, pol_a);
+              if (has0)
+                load_w_chunk<B, W_MN>(st + C::A_BYTES, &tm_w0, &full[stage], r * p.K0 + int(k0), kc, pol_w);
+              if (has1)
+                load_w_chunk<B, W_MN>(st + C::A_BYTES + C::W_BYTES, &tm_w1, &full[stage], r * p.K1 + int(k1), kc,
+                                      pol_w);
+              last_stage = stage;
+              last_phase = phase;
+            } else {
+              stage_info[stage] = info;
+              mbar_arrive(&full[stage]);
             }
+          }
+          if (++stage == C::NS) {
+            stage = 0;
+            phase ^= 1;
           }
         }
       }
-      if (!alive) {
-        // let the copies already issued land before the CTA exits
-        int st = stage, ph = phase;
-        for (int i = 0; i < C::NS && i < issued; ++i) {
-          if (--st < 0) {
-            st = C::NS - 1;
-            ph ^= 1;
-          }
-          Ctl drain_ctl{abort_flag, p.status, 100000000ull};
-          const uint32_t a = smem_u32(&full[st]);
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < drain_ctl.timeout_ns) {
-          }
+      alive = __shfl_sync(0xffffffffu, alive, 0);
+      __syncwarp();
+    }
+    if (!alive && lane == 0 && last_stage >= 0) {
+      // error path: let this warp's copies in flight land before the CTA exits
+      int st = last_stage;
+      uint32_t ph = last_phase;
+      for (int i = 0; i < C::NS; ++i) {
+        const uint32_t a = smem_u32(&full[st]);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+        if (--st < 0) {
+          st = C::NS - 1;
+          ph ^= 1;
         }
       }
     }
@@ -169,67 +214,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     // --------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_1 = idesc_bf16(kBM, B, false, W_MN);
+      constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
       constexpr uint64_t kBStep = W_MN ? (2048 >> 4) : (32 >> 4);
       const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
       const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(smem) + C::A_BYTES, 8192, 1024)
                                     : sdesc_sw128(smem_u32(smem) + C::A_BYTES, 16, 1024);
-      constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
       int stage = 0;
       uint32_t phase = 0;
       bool alive = true;
       bool issued_any = false;
       int i = 0;
       for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x, ++i) {
-        int m_unused, r;
-        unit_mr(u, p, m_unused, r);
         const int buf = i & 1;
         const uint32_t use = uint32_t(i >> 1);
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
         tc_fence_after();
         const uint32_t d0 = tmem + uint32_t(buf * C::ACC_COLS);
         const uint32_t d1 = d0 + B;
-        const int n = p.counts[r] & 0xFFFF;
-        const uint32_t* plan = p.plan + size_t(r) * p.S;
         uint32_t init0 = 0, init1 = 0;
-        for (int s = 0; s < n && alive; ++s) {
-          const uint32_t e = plan[s];
-          const bool has0 = ((e >> 16) & 0xFFu) != kNone;
-          const bool has1 = GU && (e >> 24) != kNone;
-          for (int kc = 0; kc < B / kBK; ++kc) {
-            if (!mbar_wait(&full[stage], phase, ctl)) {
-              alive = false;
-              break;
-            }
-            tc_fence_after();
-            // stage descriptors = stage-0 descriptors + constant start-address offsets
-            const uint64_t ad = a_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
-            const uint64_t bd0 = b_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
-            const uint64_t bd1 = bd0 + (C::W_BYTES >> 4);
-            const bool fused = GU && has0 && has1 && (init0 == init1);
-            if (fused) {
+        for (bool last = false; !last;) {
+          if (!mbar_wait(&full[stage], phase, ctl)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t info = stage_info[stage];
+          last = (info & kSiLast) != 0;
+          const bool has0 = (info & kSiHas0) != 0, has1 = GU && (info & kSiHas1) != 0;
+          // stage descriptors = stage-0 descriptors + constant start-address offsets
+          const uint64_t ad = a_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
+          const uint64_t bd0 = b_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
+          const uint64_t bd1 = bd0 + (C::W_BYTES >> 4);
+          if (GU && has0 && has1 && init0 == init1) {  // gate | up side by side: one MMA of N = 2B
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_2, kk > 0 ? 1u : init0);
+          } else {
+            if (has0) {
 #pragma unroll
               for (int kk = 0; kk < kBK / 16; ++kk)
-                mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_2, kk > 0 ? 1u : init0);
-            } else {
-              if (has0) {
-#pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk)
-                  mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init0);
-              }
-              if (has1) {
-#pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk)
-                  mma_bf16(d1, ad + 2 * kk, bd1 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init1);
-              }
+                mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init0);
             }
-            issued_any = true;
-            if (has0) init0 = 1;
-            if (has1) init1 = 1;
-            mma_commit(&empty[stage]);
-            if (++stage == C::NS) {
-              stage = 0;
-              phase ^= 1;
+            if (has1) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                mma_bf16(d1, ad + 2 * kk, bd1 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init1);
             }
+          }
+          issued_any = true;
+          if (has0) init0 = 1;
+          if (has1) init1 = 1;
+          mma_commit(&empty[stage]);
+          if (++stage == C::NS) {
+            stage = 0;
+            phase ^= 1;
           }
         }
         if (!alive) break;
@@ -244,19 +282,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else {
+  } else if (warp < kTmProd1) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     int i = 0;
+    int cw_next = 0;  // count word of the next unit, loaded one unit ahead
+    if (blockIdx.x < n_units) {
+      int m0, r0;
+      unit_mr(blockIdx.x, p, m0, r0);
+      cw_next = p.counts[r0];
+    }
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
       int m, r;
-        unit_mr(u, p, m, r);
+      unit_mr(u, p, m, r);
+      const int cw = cw_next;
+      if (u + int(gridDim.x) < n_units) {
+        int m2, r2;
+        unit_mr(u + gridDim.x, p, m2, r2);
+        cw_next = p.counts[r2];
+      }
       const int buf = i & 1;
       const uint32_t use = uint32_t(i >> 1);
       const bool got = mbar_wait(&acc_full[buf], use & 1u, ctl);
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
       tc_fence_after();
-      const int cw = p.counts[r];
       const bool any0 = (cw >> 16) & 1;
       const bool any1 = (cw >> 17) & 1;
       const int64_t row = int64_t(m) * kBM + q * 32 + lane;
@@ -709,7 +758,7 @@ static int check_ell(const BellEll& e, const char* name) {
 }
 
 // Weight tensor map: values [R, K, B, B] viewed as 2-D [R*K*B rows, B cols].
-static int make_w_map(CUtensorMap* m, const BellEll& e) {
+int make_w_map(CUtensorMap* m, const BellEll& e) {
   const uint64_t rows = uint64_t(e.R) * uint64_t(e.K) * uint64_t(e.B);
   // both layouts: boxes of 64 x 64 (128-byte rows); a [B_out, B_in] tile is
   // fetched as B/64 boxes of 64 N-rows
@@ -795,7 +844,7 @@ static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
   const int grid = int(units < sms ? units : sms);
-  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(a, w0, w1, p);
+  kern<<<grid, kTmThreads, C::SMEM_BYTES, stream>>>(a, w0, w1, p);
   return check_launch(GU ? "bell gate/up kernel" : "bell linear kernel");
 }
 

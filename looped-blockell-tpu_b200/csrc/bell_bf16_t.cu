@@ -16,8 +16,9 @@
 // the next unit's MMAs run.  Linear (down): one 256-column accumulator,
 // double buffered.
 //
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-9 epilogue (two per
-// TMEM lane quadrant, each owning 128 of the 256 tokens).
+// Warps: 0 and 10 TMA producers (alternate stages), 1 TMEM owner + MMA
+// issuer, 2-9 epilogue (two per TMEM lane quadrant, each owning 128 of the
+// 256 tokens).
 #include <string>
 
 #include "bell_bf16.cuh"
@@ -31,7 +32,8 @@ static constexpr int B = 128;                  // features per block-row (MMA M)
 static constexpr int TN = 256;                 // tokens per unit (MMA N)
 static constexpr int X_BYTES = TN * kBK * 2;   // 32 KB activation chunk
 static constexpr int W_BYTES = kBK * B * 2;    // 16 KB weight chunk
-static constexpr int kThr = 320;               // 10 warps
+static constexpr int kThr = 352;               // 11 warps
+static constexpr int kProd1 = 10;              // second producer warp
 
 // SPLIT (gate/up): every plan step carries one weight tile (the plan is built
 // without gate/up merging), so a stage is 48 KB and the ring 4 deep; fused
@@ -106,8 +108,8 @@ __global__ void __launch_bounds__(kThr, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
-  if (res_mma && warp >= 2) {
-    fill_identity(id_tile, threadIdx.x - 64, kThr - 64);
+  if (res_mma && warp >= 2 && warp < kProd1) {
+    fill_identity(id_tile, threadIdx.x - 64, 256);
     fence_proxy_async_smem();  // generic writes -> visible to the tensor core
   }
   tc_fence_before();
@@ -116,69 +118,89 @@ __global__ void __launch_bounds__(kThr, 1)
   const uint32_t tmem = *tmem_slot;
   const int n_units = p.n_mtiles * p.R;  // n_mtiles counts 256-token tiles
 
-  if (warp == 0) {
-    if (lane == 0) {  // -------------------------------------------- producer
-      prefetch_tmap(&tm_x);
-      prefetch_tmap(&tm_w0);
-      if (GU) prefetch_tmap(&tm_w1);
+  if (warp == 0 || warp == kProd1) {
+    if (lane == 0) {  // ------------------------------------------- producers
+      // Two producer warps take alternate stage uses (use g goes to warp
+      // g & 1): one thread issuing every copy tops out near one stage per
+      // ~450 cycles, about the MMA time of a stage.
+      const int pid = warp == 0 ? 0 : 1;
+      if (pid == 0) {
+        prefetch_tmap(&tm_x);
+        prefetch_tmap(&tm_w0);
+        if (GU || res_mma) prefetch_tmap(&tm_w1);
+      }
       const uint64_t pol_x = policy_evict_normal(), pol_w = policy_evict_last();
-      int stage = 0, issued = 0;
-      uint32_t phase = 0;
+      int stage = 0;
+      uint32_t phase = 0, g = 0;
+      int last_stage = -1;
+      uint32_t last_phase = 0;
       bool alive = true;
       for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
         int m, r;
         unit_mr(u, p, m, r);
         const int n = p.counts[r] & 0xFFFF;
         const uint32_t* plan = p.plan + size_t(r) * p.S;
-        for (int s = 0; s < n && alive; ++s) {
-          const uint32_t e = plan[s];
-          const int c = int(e & 0xFFFFu);
-          const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
-          const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
-          const uint32_t bytes = X_BYTES + (has0 ? W_BYTES : 0) + (has1 ? W_BYTES : 0);
-          for (int kc = 0; kc < B / kBK; ++kc) {
+        const int n_uses = n * (B / kBK) + (res_mma ? B / kBK : 0);
+        for (int j = 0; j < n_uses && alive; ++j, ++g) {
+          if (int(g & 1u) == pid) {
             if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
               alive = false;
               break;
             }
             uint8_t* st = smem + stage * C::STAGE;
-            mbar_arrive_expect_tx(&full[stage], bytes);
-            tma_load_2d(st, &tm_x, &full[stage], c * B + kc * kBK, m * TN, pol_x);
+            const int s = j >> 1, kc = j & 1;
+            if (s < n) {
+              const uint32_t e = plan[s];
+              const int c = int(e & 0xFFFFu);
+              const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+              const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
+              mbar_arrive_expect_tx(&full[stage], X_BYTES + (has0 ? W_BYTES : 0) + (has1 ? W_BYTES : 0));
+              tma_load_2d(st, &tm_x, &full[stage], c * B + kc * kBK, m * TN, pol_x);
 #pragma unroll
-            for (int w = 0; w < 2; ++w) {
-              if (w == 0 ? !has0 : !has1) continue;
-              const CUtensorMap* map = w == 0 ? &tm_w0 : &tm_w1;
-              const int tile = w == 0 ? r * p.K0 + int(k0) : r * p.K1 + int(k1);
-              uint8_t* dst = st + X_BYTES + (C::TWO_W ? w : 0) * W_BYTES;
+              for (int w = 0; w < 2; ++w) {
+                if (w == 0 ? !has0 : !has1) continue;
+                const CUtensorMap* map = w == 0 ? &tm_w0 : &tm_w1;
+                const int tile = w == 0 ? r * p.K0 + int(k0) : r * p.K1 + int(k1);
+                uint8_t* dst = st + X_BYTES + (C::TWO_W ? w : 0) * W_BYTES;
 #pragma unroll
-              for (int nb = 0; nb < 2; ++nb) {
-                if constexpr (W_MN) tma_load_2d(dst + nb * 8192, map, &full[stage], nb * 64, tile * B + kc * kBK, pol_w);
-                else tma_load_2d(dst + nb * 8192, map, &full[stage], kc * kBK, tile * B + nb * 64, pol_w);
+                for (int nb = 0; nb < 2; ++nb) {
+                  if constexpr (W_MN)
+                    tma_load_2d(dst + nb * 8192, map, &full[stage], nb * 64, tile * B + kc * kBK, pol_w);
+                  else
+                    tma_load_2d(dst + nb * 8192, map, &full[stage], kc * kBK, tile * B + nb * 64, pol_w);
+                }
               }
+            } else {
+              // residual columns of this block-row (tm_w1 maps the residual for linear)
+              mbar_arrive_expect_tx(&full[stage], X_BYTES);
+              tma_load_2d(st, &tm_w1, &full[stage], r * B + kc * kBK, m * TN, pol_x);
             }
-            ++issued;
-            if (++stage == C::NS) {
-              stage = 0;
-              phase ^= 1;
-            }
+            last_stage = stage;
+            last_phase = phase;
           }
-        }
-        // residual columns of this block-row (tm_w1 maps the residual for linear)
-        for (int kc = 0; res_mma && alive && kc < B / kBK; ++kc) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
-            alive = false;
-            break;
-          }
-          uint8_t* st = smem + stage * C::STAGE;
-          mbar_arrive_expect_tx(&full[stage], X_BYTES);
-          tma_load_2d(st, &tm_w1, &full[stage], r * B + kc * kBK, m * TN, pol_x);
           if (++stage == C::NS) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      (void)issued;
+      if (!alive && last_stage >= 0) {
+        // error path: let this warp's copies in flight land before the CTA exits
+        // (a stage use newer than the last one issued here belongs to the other
+        // producer; walking back over NS uses covers every copy still pending)
+        int st = last_stage;
+        uint32_t ph = last_phase;
+        for (int i = 0; i < C::NS; ++i) {
+          const uint32_t a = smem_u32(&full[st]);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+          if (--st < 0) {
+            st = C::NS - 1;
+            ph ^= 1;
+          }
+        }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ----------------------------------------- MMA issuer
@@ -265,7 +287,7 @@ __global__ void __launch_bounds__(kThr, 1)
         }
       }
     }
-  } else {
+  } else if (warp < kProd1) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3, half = (warp - 2) >> 2;
     int i = 0;

@@ -5,6 +5,7 @@
 // (csrc/loop/persistent_core.cu:315-335): normalise, run the Block-ELL
 // SwiGLU without fused residual, add the PRE-norm h.  RMSNorm follows
 // looped_blockell/layers/norms.py:8-15 (eps default 1e-5, config.py:110).
+#include <cstdlib>
 #include <string>
 
 #include "bell_host.h"
@@ -77,6 +78,17 @@ int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d,
   return check_launch("bell_rmsnorm_kernel");
 }
 
+// The persistent kernel runs the loop when the tile size is 64 and a barrier
+// workspace is given (BELL_LOOP_KERNEL=multi forces the multi-launch loop).
+static bool use_persistent_loop(const BellLoopDesc* d) {
+  static const bool multi = [] {
+    const char* e = std::getenv("BELL_LOOP_KERNEL");
+    return e && std::string(e) == "multi";
+  }();
+  return !multi && d->gate.B == 64 && d->barrier && aligned16(d->barrier) && aligned16(d->norm_gain) &&
+         d->d_model % 8 == 0;
+}
+
 }  // namespace bell
 
 using namespace bell;
@@ -141,6 +153,10 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   int32_t* status = d->status ? d->status : default_status_ptr();
   if (!status) return BELL_ERR_LAUNCH;
   if (int rc = launch_ffn_plan(&f, status, s)) return rc;
+  if (use_persistent_loop(d)) {
+    const int rc = loop_persistent_bf16(d, status, s);
+    if (rc != BELL_ERR_LAUNCH) return rc;  // no cooperative grid: run the multi-launch loop
+  }
   for (int it = 0; it < d->L; ++it) {
     if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
     if (int rc = gate_up_bf16(&f, status, s)) return rc;

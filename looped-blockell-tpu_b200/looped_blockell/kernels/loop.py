@@ -33,7 +33,7 @@ def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, 
     mid = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
     plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
                        dtype=torch.uint8, device=dev)
-    barrier = torch.zeros(64, dtype=torch.uint8, device=dev)
+    barrier = torch.empty(64, dtype=torch.uint8, device=dev)  # zero-filled by the library
     desc = _lib.BellLoopDesc()
     desc.T, desc.d_model, desc.d_ff, desc.L, desc.eps = N, d, F, int(L), float(eps)
     desc.h_in, desc.h_out = h.data_ptr(), out.data_ptr()

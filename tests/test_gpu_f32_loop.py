@@ -93,6 +93,35 @@ def test_loop_config4_row_sample():
     assert K.read_status() == 0
 
 
+@pytest.mark.parametrize("layout", [O.LAYOUT_IN_OUT, O.LAYOUT_OUT_IN])
+@pytest.mark.parametrize("T,L,dead", [(200, 3, 0), (77, 2, 6), (384, 5, 3)])
+def test_loop_edge_cases(layout, T, L, dead):
+    """Ragged token counts (partial 128-token tiles), dead slots, non-unit
+    gain, both tile layouts: the single persistent loop kernel vs the oracle
+    with the bf16 roundings of the op."""
+    K = _K()
+    case = make_case(T, 256, 512, 64, 2, 3, 4, seed=T + L, dead=dead)
+    dev = to_dev(case, torch.bfloat16, layout)
+    gain = (1.0 + 0.25 * torch.randn(256, generator=torch.Generator().manual_seed(L))).to(torch.bfloat16)
+    out = K.looped_ffn(dev["x"], gain.cuda(), dev["vg"], dev["cg"], dev["vu"], dev["cu"], dev["vd"], dev["cd"], L=L,
+                       layout=layout)
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    vt = (lambda t: np.swapaxes(f(t), -1, -2)) if layout == O.LAYOUT_OUT_IN else f
+    ref = O.looped_ffn(f(dev["x"]), f(gain), (vt(dev["vg"]), case["cg"], 0), (vt(dev["vu"]), case["cu"], 0),
+                       (vt(dev["vd"]), case["cd"], 0), L=L, round_bf16=True)
+    assert O.rel_l2(out.float().cpu().numpy(), ref) < TOL_BF16
+    assert K.read_status() == 0
+
+
+def test_loop_zero_iterations_copies_state():
+    K = _K()
+    case = make_case(130, 256, 512, 64, 2, 2, 4, seed=9)
+    dev = to_dev(case, torch.bfloat16)
+    gain = torch.ones(256, dtype=torch.bfloat16, device="cuda")
+    out = K.looped_ffn(dev["x"], gain, dev["vg"], dev["cg"], dev["vu"], dev["cu"], dev["vd"], dev["cd"], L=0)
+    assert torch.equal(out, dev["x"])
+
+
 def test_injection_matches_formula():
     K = _K()
     rng = np.random.default_rng(5)
