@@ -35,18 +35,25 @@ struct Cfg {
   static constexpr int W_BYTES = kBK * B * 2;           // 8 / 16 KB
   static constexpr int STAGE_BYTES = A_BYTES + W_BYTES * (GU ? 2 : 1);
   static constexpr int NS = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
-  static constexpr int ACC_COLS = GU ? 2 * B : B;       // fp32 columns per accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;        // double buffered
-  // align + barriers (512) + stage info (64) + two staged plan rows
-  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + 2 * kRowMax * 4;
+  static constexpr int ACC_COLS = GU ? 2 * B : B;       // fp32 columns of one accumulator
+  // two MMA issuers, each double buffered when the four accumulators fit in
+  // TMEM (all but gate/up at B = 128)
+  static constexpr int NBUF = 4 * ACC_COLS <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = 2 * NBUF * ACC_COLS < 128 ? 128 : 2 * NBUF * ACC_COLS;
+  // align + barriers (512) + stage info (64) + one staged plan row per producer
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + 4 * kRowMax * 4;
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
+  static_assert(NS % 2 == 0, "the stage ring is split between two MMA issuers");
 };
 
 
-// Single-CTA token-major kernel: warp 0 and warp 6 TMA producers, warp 1
-// TMEM owner + MMA issuer, warps 2-5 epilogue.
-static constexpr int kTmThreads = 224;
-static constexpr int kTmProd1 = 6;
+// Single-CTA token-major kernel: warps 0, 6, 7, 8 TMA producers, warps 1
+// and 9 MMA issuers (warp 1 owns TMEM), warps 2-5 epilogue.  The stage ring
+// is split in two, one per MMA issuer.
+static constexpr int kTmProds = 4;
+static constexpr int kTmProd1 = 6;  // first of the extra producer warps
+static constexpr int kTmMma1 = kTmProd1 + kTmProds - 1;  // second MMA issuer warp
+static constexpr int kTmThreads = 32 * (kTmMma1 + 1);
 
 // Load one [64 K x B] weight chunk of tile `tile` (global tile index r*K+k).
 template <int B, bool W_MN>
@@ -75,15 +82,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     bell_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w0,
                      const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
   using C = Cfg<B, GU>;
+  constexpr int NR = C::NS / 2;  // stages per ring (one ring per MMA issuer)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ctl_base = smem + C::NS * C::STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ctl_base);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctl_base);  // [ring * NR + stage]
   uint64_t* empty = full + C::NS;
-  uint64_t* acc_full = empty + C::NS;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* acc_full = empty + C::NS;  // [issuer * 2 + buf]
+  uint64_t* acc_empty = acc_full + 4;
+  uint64_t* drain = acc_empty + 4;  // one per MMA issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* stage_info = reinterpret_cast<uint32_t*>(ctl_base + 512);
   uint32_t* rows = reinterpret_cast<uint32_t*>(ctl_base + 576);  // one plan row per producer warp
@@ -97,11 +105,12 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -116,13 +125,17 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 
   const int n_units = p.n_mtiles * p.R;
   constexpr int KC = B / kBK;  // stages per plan step
+  // The CTA's units alternate between two rings / MMA issuers: its i-th unit
+  // (u = blockIdx.x + i * gridDim.x) goes to issuer i & 1.
 
-  if (warp == 0 || warp == kTmProd1) {
+  if (warp == 0 || (warp >= kTmProd1 && warp < kTmProd1 + kTmProds - 1)) {
     // ----------------------------------------------------------- producers
-    // Two producer warps take alternate stage uses (use g goes to warp g & 1).
-    // Each warp stages its plan rows through shared memory one unit ahead;
-    // lane 0 issues the copies and writes each stage's info word.
-    const int pid = warp == 0 ? 0 : 1;
+    // Producers 0, 1 fill ring 0 and producers 2, 3 ring 1; the two of a ring
+    // take its stage uses alternately (a thread needs about 200 cycles per TMA
+    // issue).  Each warp stages its plan rows through shared memory one unit
+    // ahead; its elected lane issues the copies and writes the stage info.
+    const int pid = warp == 0 ? 0 : warp - kTmProd1 + 1;
+    const int ring = pid >> 1, sub = pid & 1;
     uint32_t* row = rows + pid * kRowMax;
     if (pid == 0 && lane == 0) {
       prefetch_tmap(&tm_a);
@@ -131,120 +144,131 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
     const uint64_t pol_a = policy_evict_normal();
     const uint64_t pol_w = policy_evict_last();
-    int stage = 0;
+    int stage = 0;  // within the ring
     uint32_t phase = 0, g = 0;
     int last_stage = -1;
     uint32_t last_phase = 0;
     bool alive = true;
     RowAhead ahead;
-    if (blockIdx.x < n_units) {
+    const int u0 = blockIdx.x + ring * gridDim.x, du = 2 * gridDim.x;
+    if (u0 < n_units) {
       int m0, r0;
-      unit_mr(blockIdx.x, p, m0, r0);
+      unit_mr(u0, p, m0, r0);
       row_fetch(ahead, p.plan, p.counts, p.S, r0);
     }
-    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+    for (int u = u0; u < n_units && alive; u += du) {
       int m, r;
       unit_mr(u, p, m, r);
-      const int n = ahead.cnt & 0xFFFF;
+      const int real = (ahead.cnt & 0xFFFF) * KC;
       row_put(ahead, row, p.S);
       __syncwarp();
-      if (u + int(gridDim.x) < n_units) {
+      if (u + du < n_units) {
         int m2, r2;
-        unit_mr(u + gridDim.x, p, m2, r2);
+        unit_mr(u + du, p, m2, r2);
         row_fetch(ahead, p.plan, p.counts, p.S, r2);
       }
-      if (lane == 0) {
-        const int uses = n > 0 ? n * KC : 1;  // a unit without live steps: one empty stage
-        for (int j = 0; j < uses; ++j, ++g) {
-          if (int(g & 1u) == pid) {
-            if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
-              alive = false;
-              break;
-            }
-            uint32_t info = (j == 0 ? kSiFirst : 0u) | (j == uses - 1 ? kSiLast : 0u);
-            if (n > 0) {
-              const uint32_t e = row[j / KC];
-              const int kc = j % KC;
-              const int c = int(e & 0xFFFFu);
-              const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
-              const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
-              info |= (has0 ? kSiHas0 : 0u) | (has1 ? kSiHas1 : 0u);
-              stage_info[stage] = info;
-              uint8_t* st = smem + stage * C::STAGE_BYTES;
-              mbar_arrive_expect_tx(&full[stage],
-                                    C::A_BYTES + (has0 ? C::W_BYTES : 0) + (has1 ? C::W_BYTES : 0));
-              tma_load_2d(st, &tm_a, &full[stage], c * B + kc * kBK, m * kBM, pol_a);
+      const int uses = real > 1 ? real : 1;  // a unit without live steps: one empty stage
+      for (int j = 0; j < uses; ++j, ++g) {
+        if (int(g & 1u) == sub) {
+          const int slot = ring * NR + stage;
+          if (!__all_sync(0xffffffffu, mbar_wait(&empty[slot], phase ^ 1, ctl))) {
+            alive = false;
+            break;
+          }
+          uint32_t info = (j == 0 ? kSiFirst : 0u) | (j == uses - 1 ? kSiLast : 0u);
+          if (j < real) {
+            const uint32_t e = row[j / KC];
+            const int kc = j % KC;
+            const int c = int(e & 0xFFFFu);
+            const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+            const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
+            info |= (has0 ? kSiHas0 : 0u) | (has1 ? kSiHas1 : 0u);
+            if (elect_one()) {
+              stage_info[slot] = info;
+              uint8_t* st = smem + slot * C::STAGE_BYTES;
+              mbar_arrive_expect_tx(&full[slot], C::A_BYTES + (has0 ? C::W_BYTES : 0) + (has1 ? C::W_BYTES : 0));
+              tma_load_2d(st, &tm_a, &full[slot], c * B + kc * kBK, m * kBM, pol_a);
               if (has0)
-                load_w_chunk<B, W_MN>(st + C::A_BYTES, &tm_w0, &full[stage], r * p.K0 + int(k0), kc, pol_w);
+                load_w_chunk<B, W_MN>(st + C::A_BYTES, &tm_w0, &full[slot], r * p.K0 + int(k0), kc, pol_w);
               if (has1)
-                load_w_chunk<B, W_MN>(st + C::A_BYTES + C::W_BYTES, &tm_w1, &full[stage], r * p.K1 + int(k1), kc,
+                load_w_chunk<B, W_MN>(st + C::A_BYTES + C::W_BYTES, &tm_w1, &full[slot], r * p.K1 + int(k1), kc,
                                       pol_w);
-              last_stage = stage;
-              last_phase = phase;
-            } else {
-              stage_info[stage] = info;
-              mbar_arrive(&full[stage]);
             }
+            last_stage = slot;
+            last_phase = phase;
+          } else if (elect_one()) {
+            stage_info[slot] = info;  // empty stage: no copies
+            mbar_arrive(&full[slot]);
           }
-          if (++stage == C::NS) {
-            stage = 0;
-            phase ^= 1;
-          }
+          __syncwarp();
+        }
+        if (++stage == NR) {
+          stage = 0;
+          phase ^= 1;
         }
       }
-      alive = __shfl_sync(0xffffffffu, alive, 0);
       __syncwarp();
     }
     if (!alive && lane == 0 && last_stage >= 0) {
       // error path: let this warp's copies in flight land before the CTA exits
-      int st = last_stage;
+      int st = last_stage - ring * NR;
       uint32_t ph = last_phase;
-      for (int i = 0; i < C::NS; ++i) {
-        const uint32_t a = smem_u32(&full[st]);
+      for (int i = 0; i < NR; ++i) {
+        const uint32_t a = smem_u32(&full[ring * NR + st]);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < 100000000ull) {
         }
         if (--st < 0) {
-          st = C::NS - 1;
+          st = NR - 1;
           ph ^= 1;
         }
       }
     }
-  } else if (warp == 1) {
-    // --------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC_1 = idesc_bf16(kBM, B, false, W_MN);
-      constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
-      constexpr uint64_t kBStep = W_MN ? (2048 >> 4) : (32 >> 4);
-      const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
-      const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(smem) + C::A_BYTES, 8192, 1024)
-                                    : sdesc_sw128(smem_u32(smem) + C::A_BYTES, 16, 1024);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool alive = true;
-      bool issued_any = false;
-      int i = 0;
-      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x, ++i) {
-        const int buf = i & 1;
-        const uint32_t use = uint32_t(i >> 1);
-        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
+  } else if (warp == 1 || warp == kTmMma1) {
+    // -------------------------------------------------------- MMA issuers
+    // Issuer k takes the CTA's units i with i & 1 == k from ring k into its
+    // own (double-buffered where TMEM allows) accumulator: at tile size 64 one
+    // thread issuing every MMA is slower than the tensor core.  The whole warp
+    // runs the loop; its elected lane issues and commits.
+    const int k = warp == 1 ? 0 : 1;
+    const bool leader = elect_one();
+    constexpr uint32_t IDESC_1 = idesc_bf16(kBM, B, false, W_MN);
+    constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
+    constexpr uint64_t kBStep = W_MN ? (2048 >> 4) : (32 >> 4);
+    const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
+    const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(smem) + C::A_BYTES, 8192, 1024)
+                                  : sdesc_sw128(smem_u32(smem) + C::A_BYTES, 16, 1024);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool alive = true;
+    int ik = 0;  // units of this issuer so far
+    for (int u = blockIdx.x + k * gridDim.x; u < n_units && alive; u += 2 * gridDim.x, ++ik) {
+      const int buf = C::NBUF == 2 ? (ik & 1) : 0;
+      const uint32_t use = C::NBUF == 2 ? uint32_t(ik >> 1) : uint32_t(ik);
+      const int ab = k * 2 + buf;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[ab], (use & 1u) ^ 1u, ctl))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d0 = tmem + uint32_t((k * C::NBUF + buf) * C::ACC_COLS);
+      const uint32_t d1 = d0 + B;
+      uint32_t init0 = 0, init1 = 0;
+      for (bool last = false; !last;) {
+        const int slot = k * NR + stage;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[slot], phase, ctl))) {
+          alive = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d0 = tmem + uint32_t(buf * C::ACC_COLS);
-        const uint32_t d1 = d0 + B;
-        uint32_t init0 = 0, init1 = 0;
-        for (bool last = false; !last;) {
-          if (!mbar_wait(&full[stage], phase, ctl)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t info = stage_info[stage];
-          last = (info & kSiLast) != 0;
-          const bool has0 = (info & kSiHas0) != 0, has1 = GU && (info & kSiHas1) != 0;
-          // stage descriptors = stage-0 descriptors + constant start-address offsets
-          const uint64_t ad = a_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
-          const uint64_t bd0 = b_desc0 + uint64_t(stage) * (C::STAGE_BYTES >> 4);
-          const uint64_t bd1 = bd0 + (C::W_BYTES >> 4);
+        const uint32_t info = stage_info[slot];
+        last = (info & kSiLast) != 0;
+        const bool has0 = (info & kSiHas0) != 0, has1 = GU && (info & kSiHas1) != 0;
+        // stage descriptors = stage-0 descriptors + constant start-address offsets
+        const uint64_t ad = a_desc0 + uint64_t(slot) * (C::STAGE_BYTES >> 4);
+        const uint64_t bd0 = b_desc0 + uint64_t(slot) * (C::STAGE_BYTES >> 4);
+        const uint64_t bd1 = bd0 + (C::W_BYTES >> 4);
+        if (leader) {
           if (GU && has0 && has1 && init0 == init1) {  // gate | up side by side: one MMA of N = 2B
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
@@ -261,28 +285,30 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 mma_bf16(d1, ad + 2 * kk, bd1 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init1);
             }
           }
-          issued_any = true;
-          if (has0) init0 = 1;
-          if (has1) init1 = 1;
-          mma_commit(&empty[stage]);
-          if (++stage == C::NS) {
-            stage = 0;
-            phase ^= 1;
-          }
+          mma_commit(&empty[slot]);
         }
-        if (!alive) break;
-        mma_commit(&acc_full[buf]);
+        __syncwarp();
+        if (has0) init0 = 1;
+        if (has1) init1 = 1;
+        if (++stage == NR) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
-      if (!alive && issued_any) {
-        // drain: wait (bounded) for every MMA issued so far
-        mma_commit(drain);
-        const uint32_t a = smem_u32(drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
-        }
+      if (!alive) break;
+      if (leader) mma_commit(&acc_full[ab]);
+      __syncwarp();
+    }
+    // every MMA of this issuer has completed before TMEM is released
+    if (leader) {
+      mma_commit(&drain[k]);
+      const uint32_t a = smem_u32(&drain[k]);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
       }
     }
-  } else if (warp < kTmProd1) {
+    __syncwarp();
+  } else if (warp >= 2 && warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     int i = 0;
@@ -301,16 +327,18 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         unit_mr(u + gridDim.x, p, m2, r2);
         cw_next = p.counts[r2];
       }
-      const int buf = i & 1;
-      const uint32_t use = uint32_t(i >> 1);
-      const bool got = mbar_wait(&acc_full[buf], use & 1u, ctl);
+      const int k = i & 1, ik = i >> 1;
+      const int buf = C::NBUF == 2 ? (ik & 1) : 0;
+      const uint32_t use = C::NBUF == 2 ? uint32_t(ik >> 1) : uint32_t(ik);
+      const int ab = k * 2 + buf;
+      const bool got = mbar_wait(&acc_full[ab], use & 1u, ctl);
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
       tc_fence_after();
       const bool any0 = (cw >> 16) & 1;
       const bool any1 = (cw >> 17) & 1;
       const int64_t row = int64_t(m) * kBM + q * 32 + lane;
       const bool row_ok = row < p.T;
-      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * C::ACC_COLS);
+      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t((k * C::NBUF + buf) * C::ACC_COLS);
 #pragma unroll 1
       for (int j = 0; j < B / 32; ++j) {
         if constexpr (GU) {
@@ -397,7 +425,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   }
 
