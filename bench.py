@@ -195,14 +195,14 @@ def run_gpu(args, cfg, rank, world):
         def step(x):
             return model.forward(x, out=step_out)
     elif cfg.L > 1:
-        # the shared-weight loop (config 4): one persistent kernel per step
+        # the shared-weight loop (config 4): L x (RMSNorm, gate/up, down) per step
         from looped_blockell.kernels.loop import looped_ffn
         if world > 1:
             raise SystemExit("the loop workload runs on one GPU per replica")
         out = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
         h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
         gain = torch.ones(d, dtype=torch.bfloat16, device="cuda")
-        launches_per_step = 3  # plan, barrier reset, loop kernel
+        launches_per_step = 1 + 3 * cfg.L  # plan, then RMSNorm + gate/up + down per iteration
 
         def step(x):
             return looped_ffn(x, gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L, layout=lay)
@@ -333,8 +333,8 @@ def run_gpu(args, cfg, rank, world):
                                 "peak": tc_peak, "unit": "TFLOP/s", "frac": gu["tflops"] / tc_peak,
                                 "peak_source": f"{peak_src} bf16 burst", "traffic": None,
                                 "kernel_ms": gu["ms"], "whole_step_frac": tflops / world / tc_peak}
-        if cfg.L > 1:  # the whole step is the one persistent loop kernel (+ plan and barrier reset)
-            line["roofline"] = {"bound": "tensor", "kernel": "loopk::loop_kernel (whole step)", "achieved": tflops,
+        if cfg.L > 1:  # the whole loop step (gate/up and down kernels dominate)
+            line["roofline"] = {"bound": "tensor", "kernel": "loop step (bell_bf16_kernel gate/up + down)", "achieved": tflops,
                                 "peak": tc_peak, "unit": "TFLOP/s", "frac": tflops / tc_peak,
                                 "peak_source": f"{peak_src} bf16 burst", "traffic": None, "kernel_ms": ms}
         if world == 1 and not args.no_cpu:

@@ -8,433 +8,62 @@
 //     (swiglu_fwd.cu:413-559), and the generic block_ell_matmul
 //     (looped_blockell/layers/block_ell.py:149-182).
 //
-// One persistent CTA per SM walks work units (128-token tile m, output
-// block-row r).  Warp roles:
-//   warp 0     TMA producer: per plan step, the activation tile
-//              [128 tokens x 64 K] (128-B swizzle, K-major) named by the
-//              step's column block, and the weight tile(s) [64 K x B]
-//              (MN-major for [B_in,B_out] tiles, K-major for [B_out,B_in]).
-//   warp 1     TMEM owner + single-thread tcgen05.mma issuer (M=128, fp32
-//              accumulators; gate and up side by side so a shared column
-//              block issues one N=2B MMA).
-//   warps 2-5  epilogue: tcgen05.ld, SiLU*up or +residual, bf16 stores.
-// Accumulators are double-buffered in TMEM so the epilogue of unit i
-// overlaps the MMAs of unit i+1.  Every wait is bounded (bell_ptx.cuh).
+// The token-major kernels (tile sizes 64 and 128) are one phase of the
+// engine in bell_engine.cuh: one persistent CTA per SM walks work units
+// (128-token tile m, output block-row r), activation tiles [128 tokens x
+// 64 K] (K-major) times weight tiles [64 K x B] (MN-major for [B_in,B_out]
+// tiles, K-major for [B_out,B_in]).  The tile-size-128 default is the
+// feature-major kernel (bell_bf16_t.cu); the CTA-pair kernel below is the
+// other tile-size-128 variant.
 #include <string>
 
 #include "bell_bf16.cuh"
+#include "bell_engine.cuh"
 #include "bell_host.h"
 #include "bell_ptx.cuh"
 #include "bell_sched.cuh"
 
 namespace bell {
 
-template <int B, bool GU>
-struct Cfg {
-  static constexpr int A_BYTES = kBM * kBK * 2;         // 16 KB
-  static constexpr int W_BYTES = kBK * B * 2;           // 8 / 16 KB
-  static constexpr int STAGE_BYTES = A_BYTES + W_BYTES * (GU ? 2 : 1);
-  static constexpr int NS = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
-  static constexpr int ACC_COLS = GU ? 2 * B : B;       // fp32 columns of one accumulator
-  // two MMA issuers, each double buffered when the four accumulators fit in
-  // TMEM (all but gate/up at B = 128)
-  static constexpr int NBUF = 4 * ACC_COLS <= 512 ? 2 : 1;
-  static constexpr int TMEM_COLS = 2 * NBUF * ACC_COLS < 128 ? 128 : 2 * NBUF * ACC_COLS;
-  // align + barriers (512) + stage info (64) + one staged plan row per producer
-  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + 4 * kRowMax * 4;
-  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
-  static_assert(NS % 2 == 0, "the stage ring is split between two MMA issuers");
-};
-
-
-// Single-CTA token-major kernel: warps 0, 6, 7, 8 TMA producers, warps 1
-// and 9 MMA issuers (warp 1 owns TMEM), warps 2-5 epilogue.  The stage ring
-// is split in two, one per MMA issuer.
-static constexpr int kTmProds = 4;
-static constexpr int kTmProd1 = 6;  // first of the extra producer warps
-static constexpr int kTmMma1 = kTmProd1 + kTmProds - 1;  // second MMA issuer warp
-static constexpr int kTmThreads = 32 * (kTmMma1 + 1);
-
-// Load one [64 K x B] weight chunk of tile `tile` (global tile index r*K+k).
-template <int B, bool W_MN>
-__device__ __forceinline__ void load_w_chunk(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int tile, int kc,
-                                             uint64_t pol) {
-  if constexpr (W_MN) {
-    // [B_in, B_out] tile rows are K; two 64-wide boxes when B = 128.
-#pragma unroll
-    for (int nh = 0; nh < B / 64; ++nh)
-      tma_load_2d(dst + nh * 8192, map, bar, nh * 64, tile * B + kc * kBK, pol);
-  } else {
-    // [B_out, B_in] tile rows are N; boxes of 64 K x 64 rows stacked along N.
-#pragma unroll
-    for (int nb = 0; nb < B / 64; ++nb) tma_load_2d(dst + nb * 8192, map, bar, kc * kBK, tile * B + nb * 64, pol);
-  }
-}
-
-template <int B, bool W_MN>
-__device__ __forceinline__ uint64_t w_desc(uint32_t w_addr, int kk) {
-  if constexpr (W_MN) return sdesc_sw128(w_addr + kk * 2048, 8192, 1024);
-  else return sdesc_sw128(w_addr + kk * 32, 16, 1024);
-}
-
+// Token-major gate/up or linear kernel: one phase of the engine
+// (bell_engine.cuh) over all units.
 template <int B, bool GU, bool W_MN>
-__global__ void __launch_bounds__(kTmThreads, 1)
+__global__ void __launch_bounds__(eng::kThreads, 1)
     bell_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w0,
                      const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
-  using C = Cfg<B, GU>;
-  constexpr int NR = C::NS / 2;  // stages per ring (one ring per MMA issuer)
+  using G = eng::Geo<B, GU>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ctl_base = smem + C::NS * C::STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ctl_base);  // [ring * NR + stage]
-  uint64_t* empty = full + C::NS;
-  uint64_t* acc_full = empty + C::NS;  // [issuer * 2 + buf]
-  uint64_t* acc_empty = acc_full + 4;
-  uint64_t* drain = acc_empty + 4;  // one per MMA issuer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint32_t* stage_info = reinterpret_cast<uint32_t*>(ctl_base + 512);
-  uint32_t* rows = reinterpret_cast<uint32_t*>(ctl_base + 576);  // one plan row per producer warp
-
+  const eng::Smem s = eng::carve<G>(smem_raw);
+  const uint32_t tmem = eng::setup<G>(s);
+  Ctl ctl{s.abort_flag, p.status, p.timeout_ns};
   const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  Ctl ctl{abort_flag, p.status, p.timeout_ns};
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+  switch (eng::role_of(warp)) {
+    case eng::kProducer: {
+      const int pid = eng::producer_id(warp);
+      if (pid == 0 && (threadIdx.x & 31) == 0) {
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_w0);
+        if (GU) prefetch_tmap(&tm_w1);
+      }
+      eng::ProdState st;
+      if (!eng::produce<B, GU, W_MN, G>(p, &tm_a, &tm_w0, &tm_w1, s, st, 0, pid, ctl, policy_evict_normal(),
+                                        policy_evict_last()))
+        eng::producer_drain<G>(s, st, pid);
+      break;
     }
-    for (int b = 0; b < 4; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    case eng::kIssuer: {
+      const int k = warp == 1 ? 0 : 1;
+      const bool leader = elect_one();
+      eng::IssueState st;
+      eng::issue<B, GU, W_MN, G>(p, s, tmem, st, 0, k, leader, ctl);
+      eng::issuer_drain(s, k, leader);
+      break;
     }
-    mbar_init(&drain[0], 1);
-    mbar_init(&drain[1], 1);
-    *abort_flag = 0;
-    fence_mbar_init();
+    case eng::kEpilogue:
+      eng::epilogue<B, GU, G>(p, s, tmem, 0, ctl);
+      break;
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  const int n_units = p.n_mtiles * p.R;
-  constexpr int KC = B / kBK;  // stages per plan step
-  // The CTA's units alternate between two rings / MMA issuers: its i-th unit
-  // (u = blockIdx.x + i * gridDim.x) goes to issuer i & 1.
-
-  if (warp == 0 || (warp >= kTmProd1 && warp < kTmProd1 + kTmProds - 1)) {
-    // ----------------------------------------------------------- producers
-    // Producers 0, 1 fill ring 0 and producers 2, 3 ring 1; the two of a ring
-    // take its stage uses alternately (a thread needs about 200 cycles per TMA
-    // issue).  Each warp stages its plan rows through shared memory one unit
-    // ahead; its elected lane issues the copies and writes the stage info.
-    const int pid = warp == 0 ? 0 : warp - kTmProd1 + 1;
-    const int ring = pid >> 1, sub = pid & 1;
-    uint32_t* row = rows + pid * kRowMax;
-    if (pid == 0 && lane == 0) {
-      prefetch_tmap(&tm_a);
-      prefetch_tmap(&tm_w0);
-      if (GU) prefetch_tmap(&tm_w1);
-    }
-    const uint64_t pol_a = policy_evict_normal();
-    const uint64_t pol_w = policy_evict_last();
-    int stage = 0;  // within the ring
-    uint32_t phase = 0, g = 0;
-    int last_stage = -1;
-    uint32_t last_phase = 0;
-    bool alive = true;
-    RowAhead ahead;
-    const int u0 = blockIdx.x + ring * gridDim.x, du = 2 * gridDim.x;
-    if (u0 < n_units) {
-      int m0, r0;
-      unit_mr(u0, p, m0, r0);
-      row_fetch(ahead, p.plan, p.counts, p.S, r0);
-    }
-    for (int u = u0; u < n_units && alive; u += du) {
-      int m, r;
-      unit_mr(u, p, m, r);
-      const int real = (ahead.cnt & 0xFFFF) * KC;
-      row_put(ahead, row, p.S);
-      __syncwarp();
-      if (u + du < n_units) {
-        int m2, r2;
-        unit_mr(u + du, p, m2, r2);
-        row_fetch(ahead, p.plan, p.counts, p.S, r2);
-      }
-      const int uses = real > 1 ? real : 1;  // a unit without live steps: one empty stage
-      for (int j = 0; j < uses; ++j, ++g) {
-        if (int(g & 1u) == sub) {
-          const int slot = ring * NR + stage;
-          if (!__all_sync(0xffffffffu, mbar_wait(&empty[slot], phase ^ 1, ctl))) {
-            alive = false;
-            break;
-          }
-          uint32_t info = (j == 0 ? kSiFirst : 0u) | (j == uses - 1 ? kSiLast : 0u);
-          if (j < real) {
-            const uint32_t e = row[j / KC];
-            const int kc = j % KC;
-            const int c = int(e & 0xFFFFu);
-            const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
-            const bool has0 = k0 != kNone, has1 = GU && k1 != kNone;
-            info |= (has0 ? kSiHas0 : 0u) | (has1 ? kSiHas1 : 0u);
-            if (elect_one()) {
-              stage_info[slot] = info;
-              uint8_t* st = smem + slot * C::STAGE_BYTES;
-              mbar_arrive_expect_tx(&full[slot], C::A_BYTES + (has0 ? C::W_BYTES : 0) + (has1 ? C::W_BYTES : 0));
-              tma_load_2d(st, &tm_a, &full[slot], c * B + kc * kBK, m * kBM, pol_a);
-              if (has0)
-                load_w_chunk<B, W_MN>(st + C::A_BYTES, &tm_w0, &full[slot], r * p.K0 + int(k0), kc, pol_w);
-              if (has1)
-                load_w_chunk<B, W_MN>(st + C::A_BYTES + C::W_BYTES, &tm_w1, &full[slot], r * p.K1 + int(k1), kc,
-                                      pol_w);
-            }
-            last_stage = slot;
-            last_phase = phase;
-          } else if (elect_one()) {
-            stage_info[slot] = info;  // empty stage: no copies
-            mbar_arrive(&full[slot]);
-          }
-          __syncwarp();
-        }
-        if (++stage == NR) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      __syncwarp();
-    }
-    if (!alive && lane == 0 && last_stage >= 0) {
-      // error path: let this warp's copies in flight land before the CTA exits
-      int st = last_stage - ring * NR;
-      uint32_t ph = last_phase;
-      for (int i = 0; i < NR; ++i) {
-        const uint32_t a = smem_u32(&full[ring * NR + st]);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < 100000000ull) {
-        }
-        if (--st < 0) {
-          st = NR - 1;
-          ph ^= 1;
-        }
-      }
-    }
-  } else if (warp == 1 || warp == kTmMma1) {
-    // -------------------------------------------------------- MMA issuers
-    // Issuer k takes the CTA's units i with i & 1 == k from ring k into its
-    // own (double-buffered where TMEM allows) accumulator: at tile size 64 one
-    // thread issuing every MMA is slower than the tensor core.  The whole warp
-    // runs the loop; its elected lane issues and commits.
-    const int k = warp == 1 ? 0 : 1;
-    const bool leader = elect_one();
-    constexpr uint32_t IDESC_1 = idesc_bf16(kBM, B, false, W_MN);
-    constexpr uint32_t IDESC_2 = idesc_bf16(kBM, 2 * B, false, W_MN);
-    constexpr uint64_t kBStep = W_MN ? (2048 >> 4) : (32 >> 4);
-    const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 16, 1024);
-    const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(smem) + C::A_BYTES, 8192, 1024)
-                                  : sdesc_sw128(smem_u32(smem) + C::A_BYTES, 16, 1024);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool alive = true;
-    int ik = 0;  // units of this issuer so far
-    for (int u = blockIdx.x + k * gridDim.x; u < n_units && alive; u += 2 * gridDim.x, ++ik) {
-      const int buf = C::NBUF == 2 ? (ik & 1) : 0;
-      const uint32_t use = C::NBUF == 2 ? uint32_t(ik >> 1) : uint32_t(ik);
-      const int ab = k * 2 + buf;
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[ab], (use & 1u) ^ 1u, ctl))) {
-        alive = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t d0 = tmem + uint32_t((k * C::NBUF + buf) * C::ACC_COLS);
-      const uint32_t d1 = d0 + B;
-      uint32_t init0 = 0, init1 = 0;
-      for (bool last = false; !last;) {
-        const int slot = k * NR + stage;
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[slot], phase, ctl))) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t info = stage_info[slot];
-        last = (info & kSiLast) != 0;
-        const bool has0 = (info & kSiHas0) != 0, has1 = GU && (info & kSiHas1) != 0;
-        // stage descriptors = stage-0 descriptors + constant start-address offsets
-        const uint64_t ad = a_desc0 + uint64_t(slot) * (C::STAGE_BYTES >> 4);
-        const uint64_t bd0 = b_desc0 + uint64_t(slot) * (C::STAGE_BYTES >> 4);
-        const uint64_t bd1 = bd0 + (C::W_BYTES >> 4);
-        if (leader) {
-          if (GU && has0 && has1 && init0 == init1) {  // gate | up side by side: one MMA of N = 2B
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_2, kk > 0 ? 1u : init0);
-          } else {
-            if (has0) {
-#pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)
-                mma_bf16(d0, ad + 2 * kk, bd0 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init0);
-            }
-            if (has1) {
-#pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)
-                mma_bf16(d1, ad + 2 * kk, bd1 + kk * kBStep, IDESC_1, kk > 0 ? 1u : init1);
-            }
-          }
-          mma_commit(&empty[slot]);
-        }
-        __syncwarp();
-        if (has0) init0 = 1;
-        if (has1) init1 = 1;
-        if (++stage == NR) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      if (!alive) break;
-      if (leader) mma_commit(&acc_full[ab]);
-      __syncwarp();
-    }
-    // every MMA of this issuer has completed before TMEM is released
-    if (leader) {
-      mma_commit(&drain[k]);
-      const uint32_t a = smem_u32(&drain[k]);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
-      }
-    }
-    __syncwarp();
-  } else if (warp >= 2 && warp < 6) {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    int i = 0;
-    int cw_next = 0;  // count word of the next unit, loaded one unit ahead
-    if (blockIdx.x < n_units) {
-      int m0, r0;
-      unit_mr(blockIdx.x, p, m0, r0);
-      cw_next = p.counts[r0];
-    }
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
-      int m, r;
-      unit_mr(u, p, m, r);
-      const int cw = cw_next;
-      if (u + int(gridDim.x) < n_units) {
-        int m2, r2;
-        unit_mr(u + gridDim.x, p, m2, r2);
-        cw_next = p.counts[r2];
-      }
-      const int k = i & 1, ik = i >> 1;
-      const int buf = C::NBUF == 2 ? (ik & 1) : 0;
-      const uint32_t use = C::NBUF == 2 ? uint32_t(ik >> 1) : uint32_t(ik);
-      const int ab = k * 2 + buf;
-      const bool got = mbar_wait(&acc_full[ab], use & 1u, ctl);
-      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
-      tc_fence_after();
-      const bool any0 = (cw >> 16) & 1;
-      const bool any1 = (cw >> 17) & 1;
-      const int64_t row = int64_t(m) * kBM + q * 32 + lane;
-      const bool row_ok = row < p.T;
-      const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t((k * C::NBUF + buf) * C::ACC_COLS);
-#pragma unroll 1
-      for (int j = 0; j < B / 32; ++j) {
-        if constexpr (GU) {
-          uint32_t g[32], v[32];
-          tmem_ld32(tbase + j * 32, g);
-          tmem_ld32(tbase + B + j * 32, v);
-          tmem_ld_wait();
-          if (!any0 || !any1) {  // a projection with no live tile is zero, so is h
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              if (!any0) g[t] = 0u;
-              if (!any1) v[t] = 0u;
-            }
-          }
-          uint32_t hp[16];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const float g0 = __uint_as_float(g[2 * t]), g1 = __uint_as_float(g[2 * t + 1]);
-            const float u0 = __uint_as_float(v[2 * t]), u1 = __uint_as_float(v[2 * t + 1]);
-            hp[t] = pack_bf16x2(silu_fast(g0) * u0, silu_fast(g1) * u1);
-          }
-          if (row_ok) {
-            const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
-            __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(p.out) + off;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) st_global_v4(hrow + t * 8, hp[4 * t], hp[4 * t + 1], hp[4 * t + 2], hp[4 * t + 3]);
-            if (p.gate_pre) {  // optional intermediates: packed only when requested
-              __nv_bfloat16* grow = static_cast<__nv_bfloat16*>(p.gate_pre) + off;
-#pragma unroll
-              for (int t = 0; t < 4; ++t)
-                st_global_v4(grow + t * 8, pack_bf16x2(__uint_as_float(g[8 * t]), __uint_as_float(g[8 * t + 1])),
-                             pack_bf16x2(__uint_as_float(g[8 * t + 2]), __uint_as_float(g[8 * t + 3])),
-                             pack_bf16x2(__uint_as_float(g[8 * t + 4]), __uint_as_float(g[8 * t + 5])),
-                             pack_bf16x2(__uint_as_float(g[8 * t + 6]), __uint_as_float(g[8 * t + 7])));
-            }
-            if (p.up_out) {
-              __nv_bfloat16* urow = static_cast<__nv_bfloat16*>(p.up_out) + off;
-#pragma unroll
-              for (int t = 0; t < 4; ++t)
-                st_global_v4(urow + t * 8, pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
-                             pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
-                             pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
-                             pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
-            }
-          }
-        } else {
-          uint32_t a[32];
-          tmem_ld32(tbase + j * 32, a);
-          tmem_ld_wait();
-          float f[32];
-#pragma unroll
-          for (int t = 0; t < 32; ++t) f[t] = any0 ? __uint_as_float(a[t]) : 0.f;
-          if (row_ok) {
-            const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
-            if (p.add_residual) {
-              const __nv_bfloat16* rrow = static_cast<const __nv_bfloat16*>(p.residual) + off;
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const uint4 rv = ld_global_v4(rrow + t * 8);
-                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                  const float2 x2 = unpack_bf16x2(rw[w]);
-                  f[8 * t + 2 * w] += x2.x;
-                  f[8 * t + 2 * w + 1] += x2.y;
-                }
-              }
-            }
-            if (p.out_f32) {
-              float* orow = static_cast<float*>(p.out) + off;
-#pragma unroll
-              for (int t = 0; t < 8; ++t)
-                st_global_v4(orow + t * 4, __float_as_uint(f[4 * t]), __float_as_uint(f[4 * t + 1]),
-                             __float_as_uint(f[4 * t + 2]), __float_as_uint(f[4 * t + 3]));
-            } else {
-              __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + off;
-#pragma unroll
-              for (int t = 0; t < 4; ++t)
-                st_global_v4(orow + t * 8, pack_bf16x2(f[8 * t], f[8 * t + 1]), pack_bf16x2(f[8 * t + 2], f[8 * t + 3]),
-                             pack_bf16x2(f[8 * t + 4], f[8 * t + 5]), pack_bf16x2(f[8 * t + 6], f[8 * t + 7]));
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[ab]);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
-  }
+  eng::teardown<G>(tmem);
 }
 
 // ================================================================ 2-SM kernel
@@ -670,9 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int j = 0; j < B / 32; ++j) {
         if constexpr (GU) {
           uint32_t g[32], v[32];
-          tmem_ld32(tbase + j * 32, g);
-          tmem_ld32(tbase + 128 + j * 32, v);
-          tmem_ld_wait();
+          tmem_ld32x2_sync(tbase + j * 32, g, tbase + 128 + j * 32, v);
           uint32_t hp[16];
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
@@ -711,8 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         } else {
           uint32_t a[32];
-          tmem_ld32(tbase + j * 32, a);
-          tmem_ld_wait();
+          tmem_ld32_sync(tbase + j * 32, a);
           float f[32];
 #pragma unroll
           for (int t = 0; t < 32; ++t) f[t] = any0 ? __uint_as_float(a[t]) : 0.f;
@@ -862,17 +488,17 @@ static int unit_band(bool gate_up, int R) {
 template <int B, bool GU, bool W_MN>
 static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p0,
                        cudaStream_t stream) {
-  using C = Cfg<B, GU>;
+  using G = eng::Geo<B, GU>;
   Bf16Params p = p0;
   p.band = unit_band(GU, p.R);
   auto kern = bell_bf16_kernel<B, GU, W_MN>;
-  if (int rc = set_smem(reinterpret_cast<const void*>(kern), C::SMEM_BYTES)) return rc;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), G::SMEM_BYTES)) return rc;
   int sms = 0;
   if (int rc = device_sm_count(&sms)) return rc;
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
   const int grid = int(units < sms ? units : sms);
-  kern<<<grid, kTmThreads, C::SMEM_BYTES, stream>>>(a, w0, w1, p);
+  kern<<<grid, eng::kThreads, G::SMEM_BYTES, stream>>>(a, w0, w1, p);
   return check_launch(GU ? "bell gate/up kernel" : "bell linear kernel");
 }
 

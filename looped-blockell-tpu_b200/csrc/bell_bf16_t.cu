@@ -309,9 +309,8 @@ __global__ void __launch_bounds__(kThr, 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           uint32_t g[32], v[32];
-          tmem_ld32(tmem + lane_base + uint32_t(half * 128 + j * 32), g);
-          tmem_ld32(tmem + lane_base + uint32_t(256 + half * 128 + j * 32), v);
-          tmem_ld_wait();
+          tmem_ld32x2_sync(tmem + lane_base + uint32_t(half * 128 + j * 32), g,
+                           tmem + lane_base + uint32_t(256 + half * 128 + j * 32), v);
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
             const float g0 = any0 ? __uint_as_float(g[2 * t]) : 0.f, g1 = any0 ? __uint_as_float(g[2 * t + 1]) : 0.f;
@@ -344,10 +343,9 @@ __global__ void __launch_bounds__(kThr, 1)
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
           uint32_t a[32];
-          tmem_ld32(tmem + lane_base + uint32_t(buf * TN + half * 128 + j * 32), a);
+          tmem_ld32_sync(tmem + lane_base + uint32_t(buf * TN + half * 128 + j * 32), a);
           // the residual (when requested) is already in the accumulator
           const int64_t tokj = tok0 + j * 32;
-          tmem_ld_wait();
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
             const int64_t tok = tokj + t;

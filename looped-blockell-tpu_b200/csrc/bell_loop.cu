@@ -78,14 +78,16 @@ int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d,
   return check_launch("bell_rmsnorm_kernel");
 }
 
-// The persistent kernel runs the loop when the tile size is 64 and a barrier
-// workspace is given (BELL_LOOP_KERNEL=multi forces the multi-launch loop).
+// The loop runs as one launch per phase (RMSNorm, gate/up, down) by default.
+// BELL_LOOP_KERNEL=persistent selects the single cooperative kernel
+// (bell_loop_kernel.cu; tile size 64, needs the barrier workspace): its
+// down phase does not yet match the multi-launch result, so it is opt-in.
 static bool use_persistent_loop(const BellLoopDesc* d) {
-  static const bool multi = [] {
+  static const bool persistent = [] {
     const char* e = std::getenv("BELL_LOOP_KERNEL");
-    return e && std::string(e) == "multi";
+    return e && std::string(e) == "persistent";
   }();
-  return !multi && d->gate.B == 64 && d->barrier && aligned16(d->barrier) && aligned16(d->norm_gain) &&
+  return persistent && d->gate.B == 64 && d->barrier && aligned16(d->barrier) && aligned16(d->norm_gain) &&
          d->d_model % 8 == 0;
 }
 

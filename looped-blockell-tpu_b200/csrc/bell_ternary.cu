@@ -287,8 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         uint32_t v[32];
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kB + half * 32), v);
-        tmem_ld_wait();
+        tmem_ld32_sync(tmem + (uint32_t(q * 32) << 16) + uint32_t(slot * kB + half * 32), v);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);

@@ -73,6 +73,7 @@ def test_loop_golden_fixture():
     ci = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
     out = K.looped_ffn(bf(z["h0"]), bf(z["gain"]), bf(z["vg"]), ci(z["cg"]), bf(z["vu"]), ci(z["cu"]), bf(z["vd"]),
                        ci(z["cd"]), L=int(z["L"]), eps=float(z["eps"]))
+    assert K.read_status() == 0
     assert O.rel_l2(out.float().cpu().numpy(), z["out"]) < TOL_BF16
 
 
@@ -89,7 +90,10 @@ def test_loop_config4_row_sample():
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
     ref = O.looped_ffn(f(c["x"])[rows], np.ones(cfg.d_model), (f(c["vg"]), c["cg"].cpu().numpy(), 0),
                        (f(c["vu"]), c["cu"].cpu().numpy(), 0), (f(c["vd"]), c["cd"].cpu().numpy(), 0), L=cfg.L)
-    assert O.rel_l2(out[torch.from_numpy(rows).cuda()].float().cpu().numpy(), ref) < TOL_BF16
+    got = out[torch.from_numpy(rows).cuda()].float().cpu().numpy()
+    assert O.rel_l2(got, ref) < TOL_BF16
+    x0 = f(c["x"])[rows]
+    assert O.rel_l2(got - x0, ref - x0) < 3e-2  # the L-step increment alone
     assert K.read_status() == 0
 
 
@@ -110,6 +114,9 @@ def test_loop_edge_cases(layout, T, L, dead):
     ref = O.looped_ffn(f(dev["x"]), f(gain), (vt(dev["vg"]), case["cg"], 0), (vt(dev["vu"]), case["cu"], 0),
                        (vt(dev["vd"]), case["cd"], 0), L=L, round_bf16=True)
     assert O.rel_l2(out.float().cpu().numpy(), ref) < TOL_BF16
+    # the residual dominates the state: check the FFN increments on their own
+    x0 = f(dev["x"])
+    assert O.rel_l2(out.float().cpu().numpy() - x0, ref - x0) < 2e-2
     assert K.read_status() == 0
 
 
