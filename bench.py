@@ -83,6 +83,14 @@ class ClockSampler:
         return out
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate/up launch, from ncu captures
+# of the same command on a B200.  Config 5 is captured at T=32768 (x 256 MiB) and scaled by the
+# units of a full launch (x8): the kernel walks the same unit order, so traffic grows in proportion.
+GU_DRAM_BYTES = {(5, 262144): 8 * (1.393575e9 + 1.053188e9), (2, 32768): 5.45283e8 + 4.99361e8}
+GU_DRAM_NOTE = {5: "ncu --set full at T=32768, scaled x8 by units",
+                2: "ncu --set full on the full config-2 launch"}
+
+
 def cpu_baseline_sample(cfg, tokens: int, reps: int = 1):
     """Time the oracle (numpy restatement of the reference gather+GEMM path)
     on `tokens` tokens of `cfg` using every host core; returns tokens/s."""
@@ -329,9 +337,12 @@ def run_gpu(args, cfg, rank, world):
             "clocks": clk.summary(), "e2e": e2e,
         }
         if gu:
-            line["roofline"] = {"bound": "tensor", "kernel": "bell_bf16_kernel<gate/up>", "achieved": gu["tflops"],
+            traffic = GU_DRAM_BYTES.get((args.config, cfg.T))
+            line["roofline"] = {"bound": "tensor", "kernel": "gate/up kernel (bell_bf16_fmajor_kernel at B=128, "
+                                "bell_bf16_kernel at B=64)", "achieved": gu["tflops"],
                                 "peak": tc_peak, "unit": "TFLOP/s", "frac": gu["tflops"] / tc_peak,
-                                "peak_source": f"{peak_src} bf16 burst", "traffic": None,
+                                "peak_source": f"{peak_src} bf16 burst", "traffic": traffic,
+                                "traffic_source": GU_DRAM_NOTE.get(args.config) if traffic else None,
                                 "kernel_ms": gu["ms"], "whole_step_frac": tflops / world / tc_peak}
         if cfg.L > 1:  # the whole loop step (gate/up and down kernels dominate)
             line["roofline"] = {"bound": "tensor", "kernel": "loop step (bell_bf16_kernel gate/up + down)", "achieved": tflops,
