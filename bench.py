@@ -296,14 +296,31 @@ def run_gpu(args, cfg, rank, world):
         gu = dict(ms=gu_ms, tflops=gu_flops / (gu_ms / 1e3) / 1e12)
 
     # end to end through the public op with host buffers
+    # (one GPU: the public host-buffer op, which pipelines the copies of token
+    # chunks with their compute on three streams; several GPUs: copy in, the
+    # sharded forward, copy this rank's token slice out)
     e2e = None
     if not args.no_e2e:
         xh = x.cpu().pin_memory()
         oh = torch.empty((T if world == 1 else step_out.shape[0], d), dtype=torch.bfloat16).pin_memory()
         xd = torch.empty_like(x)
+        if world == 1:
+            from looped_blockell.kernels import stream as kstream
+            if cfg.L > 1:
+                def e2e_step():
+                    kstream.looped_ffn_host(xh, gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L,
+                                            layout=lay, out_host=oh)
+            else:
+                def e2e_step():
+                    kstream.block_ell_swiglu_fwd_host(xh, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"],
+                                                      add_residual=True, layout=lay,
+                                                      shared_topology=args.shared_gate_up, out_host=oh)
+        else:
+            def e2e_step():
+                xd.copy_(xh, non_blocking=True)
+                oh.copy_(step(xd), non_blocking=True)
         for _ in range(2):
-            xd.copy_(xh, non_blocking=True)
-            oh.copy_(step(xd), non_blocking=True)
+            e2e_step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -311,8 +328,7 @@ def run_gpu(args, cfg, rank, world):
         n_e2e = max(3, min(args.steps, 5))
         a0.record()
         for _ in range(n_e2e):
-            xd.copy_(xh, non_blocking=True)
-            oh.copy_(step(xd), non_blocking=True)
+            e2e_step()
         a1.record()
         torch.cuda.synchronize()
         ems = a0.elapsed_time(a1) / n_e2e

@@ -14,7 +14,7 @@ from .ops import TILE_IN_OUT, _check_cuda, _ell, _prep_ell, _stream, plan_bytes,
 
 
 def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, L: int,
-               eps: float = 1e-5, layout: int = TILE_IN_OUT) -> torch.Tensor:
+               eps: float = 1e-5, layout: int = TILE_IN_OUT, out: torch.Tensor = None) -> torch.Tensor:
     """L iterations of ``h = h + FFN(RMSNorm(h))`` with one weight set (bf16)."""
     lib = _lib.load()
     _check_cuda("h", h)
@@ -28,7 +28,10 @@ def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, 
     B = vg.shape[2]
     F = vg.shape[0] * B
     dev = h.device
-    out = torch.empty_like(h)
+    if out is None:
+        out = torch.empty_like(h)
+    elif out.shape != h.shape or out.dtype != h.dtype or not out.is_contiguous() or out.device != h.device:
+        raise RuntimeError("out must be a contiguous tensor like h")
     hn = torch.empty_like(h)
     mid = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
     plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
