@@ -202,6 +202,19 @@ def run_gpu(args, cfg, rank, world):
 
         def step(x):
             return model.forward(x, out=step_out)
+    elif cfg.dtype == "ternary":
+        # config 3: ternary weights (2-bit packed tiles + per-tile scales), int8 activations
+        from looped_blockell.kernels.ternary import make_ternary, ternary_swiglu_fwd
+        if world > 1:
+            raise SystemExit("the ternary workload runs on one GPU per replica")
+        tg = make_ternary(c["vg"], c["cg"], d // cfg.B)
+        tu = make_ternary(c["vu"], c["cu"], d // cfg.B)
+        td = make_ternary(c["vd"], c["cd"], F // cfg.B)
+        c["x"] = c["x"].to(torch.bfloat16)
+        launches_per_step = 5  # plan, quantise x, gate/up, quantise h, down
+
+        def step(x):
+            return ternary_swiglu_fwd(x, tg, tu, td, add_residual=True)
     elif cfg.L > 1:
         # the shared-weight loop (config 4): L x (RMSNorm, gate/up, down) per step
         from looped_blockell.kernels.loop import looped_ffn
@@ -265,7 +278,7 @@ def run_gpu(args, cfg, rank, world):
 
     # dominant kernel: the fused gate/up kernel, timed alone with events
     gu = None
-    if world == 1 and cfg.L == 1:
+    if world == 1 and cfg.L == 1 and cfg.dtype == "bf16":
         from looped_blockell.kernels import _lib
         import ctypes as C
         lib = _lib.load()
@@ -300,7 +313,7 @@ def run_gpu(args, cfg, rank, world):
     # chunks with their compute on three streams; several GPUs: copy in, the
     # sharded forward, copy this rank's token slice out)
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and cfg.dtype == "bf16":
         xh = x.cpu().pin_memory()
         oh = torch.empty((T if world == 1 else step_out.shape[0], d), dtype=torch.bfloat16).pin_memory()
         xd = torch.empty_like(x)
@@ -343,7 +356,8 @@ def run_gpu(args, cfg, rank, world):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "int8 (ternary weights)" if cfg.dtype == "ternary" else "bf16",
+            "data": "synthetic",
             "config": {"workload": cfg.name, "T": T, "d_model": d, "d_ff": F, "B": cfg.B, "density": cfg.density,
                        "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
                        "parallelism": f"dff{world}" if world > 1 else "single",

@@ -80,8 +80,10 @@ int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d,
 
 // The loop runs as one launch per phase (RMSNorm, gate/up, down) by default.
 // BELL_LOOP_KERNEL=persistent selects the single cooperative kernel
-// (bell_loop_kernel.cu; tile size 64, needs the barrier workspace): its
-// down phase does not yet match the multi-launch result, so it is opt-in.
+// (bell_loop_kernel.cu; tile size 64, needs the barrier workspace).  It gives
+// the same results but is slower on B200 (config 4: 1.36 ms against 0.86 ms):
+// its 3 L grid barriers drain and refill the pipelines as the launch
+// boundaries do, and its down phase runs on the shallower gate/up ring.
 static bool use_persistent_loop(const BellLoopDesc* d) {
   static const bool persistent = [] {
     const char* e = std::getenv("BELL_LOOP_KERNEL");

@@ -114,11 +114,32 @@ __device__ __forceinline__ void norm_phase(const LoopParams& p) {
   }
 }
 
+// The engine's role functions are called through these non-inlined wrappers.
+// With the producer, issuer and epilogue of both phases all inlined into one
+// kernel body, the down phase computed wrong results (while each phase alone
+// was exact); any one role kept out of line gives exact results, so all are.
+template <bool GU, bool W_MN>
+__device__ __noinline__ bool loop_produce(const Bf16Params& p, const CUtensorMap* ta, const CUtensorMap* tw0,
+                                          const CUtensorMap* tw1, const eng::Smem& s, eng::ProdState& st, int i_base,
+                                          int pid, const Ctl& ctl, uint64_t pol_a, uint64_t pol_w) {
+  return eng::produce<B, GU, W_MN, G>(p, ta, tw0, tw1, s, st, i_base, pid, ctl, pol_a, pol_w);
+}
+template <bool GU, bool W_MN>
+__device__ __noinline__ bool loop_issue(const Bf16Params& p, const eng::Smem& s, uint32_t tmem, eng::IssueState& st,
+                                        int i_base, int k, bool leader, const Ctl& ctl) {
+  return eng::issue<B, GU, W_MN, G>(p, s, tmem, st, i_base, k, leader, ctl);
+}
+template <bool GU>
+__device__ __noinline__ bool loop_epilogue(const Bf16Params& p, const eng::Smem& s, uint32_t tmem, int i_base,
+                                           const Ctl& ctl) {
+  return eng::epilogue<B, GU, G>(p, s, tmem, i_base, ctl);
+}
+
 template <bool W_MN>
 __global__ void __launch_bounds__(eng::kThreads, 1)
     loop_kernel(const __grid_constant__ CUtensorMap tm_hn, const __grid_constant__ CUtensorMap tm_hmid,
                 const __grid_constant__ CUtensorMap tm_wg, const __grid_constant__ CUtensorMap tm_wu,
-                const __grid_constant__ CUtensorMap tm_wd, const LoopParams p) {
+                const __grid_constant__ CUtensorMap tm_wd, const __grid_constant__ LoopParams p) {
   extern __shared__ uint8_t smem_raw[];
   const eng::Smem s = eng::carve<G>(smem_raw);
   const uint32_t tmem = eng::setup<G>(s);
@@ -153,16 +174,15 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
     for (int ph = 0; ph < 2; ++ph) {
       bool role_ok = true;
       if (role == eng::kProducer) {
-        role_ok = ph == 0 ? eng::produce<B, true, W_MN, G>(p.gu, &tm_hn, &tm_wg, &tm_wu, s, ps, base, pid, ctl, pol_a,
-                                                           pol_w)
-                          : eng::produce<B, false, W_MN, G>(p.dn, &tm_hmid, &tm_wd, &tm_wd, s, ps, base + nl_gu, pid,
-                                                            ctl, pol_a, pol_w);
+        role_ok = ph == 0 ? loop_produce<true, W_MN>(p.gu, &tm_hn, &tm_wg, &tm_wu, s, ps, base, pid, ctl, pol_a, pol_w)
+                          : loop_produce<false, W_MN>(p.dn, &tm_hmid, &tm_wd, &tm_wd, s, ps, base + nl_gu, pid, ctl,
+                                                      pol_a, pol_w);
       } else if (role == eng::kIssuer) {
-        role_ok = ph == 0 ? eng::issue<B, true, W_MN, G>(p.gu, s, tmem, is, base, k, leader, ctl)
-                          : eng::issue<B, false, W_MN, G>(p.dn, s, tmem, is, base + nl_gu, k, leader, ctl);
+        role_ok = ph == 0 ? loop_issue<true, W_MN>(p.gu, s, tmem, is, base, k, leader, ctl)
+                          : loop_issue<false, W_MN>(p.dn, s, tmem, is, base + nl_gu, k, leader, ctl);
       } else {
-        role_ok = ph == 0 ? eng::epilogue<B, true, G>(p.gu, s, tmem, base, ctl)
-                          : eng::epilogue<B, false, G>(p.dn, s, tmem, base + nl_gu, ctl);
+        role_ok = ph == 0 ? loop_epilogue<true>(p.gu, s, tmem, base, ctl)
+                          : loop_epilogue<false>(p.dn, s, tmem, base + nl_gu, ctl);
       }
       if (!grid_sync(p, unsigned(3 * it + 2 + ph) * nG, ctl, !role_ok)) {
         ok = false;
