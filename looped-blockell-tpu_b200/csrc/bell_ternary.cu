@@ -18,6 +18,7 @@
 
 #include "bell_host.h"
 #include "bell_ptx.cuh"
+#include "bell_sched.cuh"
 
 namespace bell {
 namespace tern {
@@ -26,11 +27,12 @@ static constexpr int kB = 64;        // tile size supported by the ternary path
 static constexpr int kBM = 128;      // tokens per unit
 static constexpr int kA = kBM * kB;  // int8 activation tile bytes (8 KB)
 static constexpr int kW = kB * kB;   // unpacked int8 weight tile bytes (4 KB)
-static constexpr int kStage = 12288; // A + W, 1024-aligned
+static constexpr int kP = kB * kB / 4;  // packed 2-bit weight tile bytes (1 KB)
+static constexpr int kStage = kA + kW + kP;  // 13 KB, 1024-aligned
 static constexpr int kNS = 12;
 static constexpr int kSlots = 8;     // TMEM result slots of 64 columns
 static constexpr int kThreads = 448; // 14 warps
-static constexpr int kSmem = kNS * kStage + 1024 + 1024;
+static constexpr int kSmem = kNS * kStage + 1024 + 1024 + 8 * kRowMax * 4;
 
 // ------------------------------------------------------------ quantisation
 
@@ -115,8 +117,9 @@ struct TernParams {
   uint64_t timeout_ns;
 };
 
-// Warp roles: 0 TMA producer (activation tiles), 1 TMEM owner + MMA issuer,
-// 2-5 weight unpackers, 6-13 epilogue (two warps per TMEM lane quadrant, each
+// Warp roles: 0 TMA producer (activation tile and packed weight tile of each
+// step, into the stage), 1 TMEM owner + MMA issuer, 2-5 weight unpackers
+// (packed tile in shared memory -> int8 tile), 6-13 epilogue (two warps per TMEM lane quadrant, each
 // owning 32 of the 64 result columns).  Every plan step is one (column
 // block, weight tile) pair of ONE matrix; results land in one of 8 TMEM slots
 // of 64 int32 columns and are consumed in plan order.
@@ -127,10 +130,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kNS * kStage);
   uint64_t* empty = full + kNS;
-  uint64_t* tfull = empty + kNS;
+  uint64_t* pfull = empty + kNS;  // the packed weight tile of a stage has landed
+  uint64_t* tfull = pfull + kNS;
   uint64_t* tempty = tfull + kSlots;
   uint64_t* drain = tempty + kSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* epi_scales = reinterpret_cast<float*>(smem + kNS * kStage + 1024);  // [8 epilogue warps][kRowMax]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   Ctl ctl{abort_flag, p.status, p.timeout_ns};
@@ -139,6 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kNS; ++s) {
       mbar_init(&full[s], 2);  // producer (A bytes) + unpack group
       mbar_init(&empty[s], 1);
+      mbar_init(&pfull[s], 1);
     }
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&tfull[s], 1);
@@ -162,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // -------------------------------------------- producer
       prefetch_tmap(&tm_a);
       const uint64_t pol = policy_evict_normal();
+      const uint64_t pol_w = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       bool alive = true;
@@ -169,13 +176,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m = u / p.R, r = u % p.R;
         const int n = p.counts[r] & 0xFFFF;
         for (int s = 0; s < n; ++s) {
-          const int c = int(p.plan[size_t(r) * p.S + s] & 0xFFFFu);
+          const uint32_t e = p.plan[size_t(r) * p.S + s];
+          const int c = int(e & 0xFFFFu);
+          const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+          const uint8_t* src = (k0 != 255u) ? p.packed0 + (size_t(r) * p.K0 + k0) * kP
+                                            : p.packed1 + (size_t(r) * p.K1 + k1) * kP;
           if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
             alive = false;
             break;
           }
+          uint8_t* st = smem + stage * kStage;
+          mbar_arrive_expect_tx(&pfull[stage], kP);
+          bulk_load(st + kA + kW, src, kP, &pfull[stage], pol_w);
           mbar_arrive_expect_tx(&full[stage], kA);
-          tma_load_2d(smem + stage * kStage, &tm_a, &full[stage], c * kB, m * kBM, pol);
+          tma_load_2d(st, &tm_a, &full[stage], c * kB, m * kBM, pol);
           if (++stage == kNS) {
             stage = 0;
             phase ^= 1;
@@ -184,49 +198,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // ----------------------------------------- MMA issuer
-      constexpr uint32_t IDESC = idesc_s8(kBM, kB, false, false);
-      int stage = 0, slot = 0;
-      uint32_t phase = 0, sphase = 0;
-      bool alive = true, any = false;
-      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
-        const int r = u % p.R;
-        const int n = p.counts[r] & 0xFFFF;
-        for (int s = 0; s < n && alive; ++s) {
-          if (!mbar_wait(&tempty[slot], sphase ^ 1, ctl) || !mbar_wait(&full[stage], phase, ctl)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * kStage);
-          const uint32_t w_addr = a_addr + kA;
+    // --------------------------------------------------------- MMA issuer
+    // The whole warp runs the loop (warp-uniform state); the elected lane issues.
+    const bool leader = elect_one();
+    constexpr uint32_t IDESC = idesc_s8(kBM, kB, false, false);
+    int stage = 0, slot = 0;
+    uint32_t phase = 0, sphase = 0;
+    bool alive = true;
+    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+      const int r = u % p.R;
+      const int n = p.counts[r] & 0xFFFF;
+      for (int s = 0; s < n && alive; ++s) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&tempty[slot], sphase ^ 1, ctl) && mbar_wait(&full[stage], phase, ctl))) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + stage * kStage);
+        const uint32_t w_addr = a_addr + kA;
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < kB / 32; ++kk)
             mma_i8(tmem + uint32_t(slot * kB), sdesc_sw64(a_addr + kk * 32, 16, 512),
                    sdesc_sw64(w_addr + kk * 32, 16, 512), IDESC, kk > 0 ? 1u : 0u);
-          any = true;
           mma_commit(&empty[stage]);
           mma_commit(&tfull[slot]);
-          if (++stage == kNS) {
-            stage = 0;
-            phase ^= 1;
-          }
-          if (++slot == kSlots) {
-            slot = 0;
-            sphase ^= 1;
-          }
         }
-      }
-      if (!alive && any) {
-        mma_commit(drain);
-        const uint32_t a = smem_u32(drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        __syncwarp();
+        if (++stage == kNS) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++slot == kSlots) {
+          slot = 0;
+          sphase ^= 1;
         }
       }
     }
+    // every MMA has completed before TMEM is released
+    if (leader) {
+      mma_commit(drain);
+      const uint32_t a = smem_u32(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
+      }
+    }
+    __syncwarp();
   } else if (warp < 6) {
     // ------------------------------------------------------- weight unpack
+    // The producer copied the stage's packed tile next to it (pfull); the
+    // group expands it into the int8 tile the MMA reads.
     const int t = threadIdx.x - 64;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
@@ -235,22 +256,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = p.counts[r] & 0xFFFF;
       bool alive = true;
       for (int s = 0; s < n; ++s) {
-        const uint32_t e = p.plan[size_t(r) * p.S + s];
-        const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
-        const uint8_t* src = (k0 != 255u) ? p.packed0 + (size_t(r) * p.K0 + k0) * (kB * kB / 4)
-                                          : p.packed1 + (size_t(r) * p.K1 + k1) * (kB * kB / 4);
-        mbar_wait(&empty[stage], phase ^ 1, ctl);
+        mbar_wait(&pfull[stage], phase, ctl);
         asm volatile("bar.sync 1, 128;" ::: "memory");  // one abort decision for the whole group
         if (*abort_flag) {
           alive = false;
           break;
         }
         uint8_t* w = smem + stage * kStage + kA;
+        const uint32_t* packed = reinterpret_cast<const uint32_t*>(w + kW);
 #pragma unroll
         for (int i = 0; i < 2; ++i) {  // 256 words per tile, 2 per thread
           const int widx = t + i * 128;
           const int nrow = widx >> 2, c = widx & 3;
-          const uint32_t word = __ldg(reinterpret_cast<const uint32_t*>(src) + widx);
+          const uint32_t word = packed[widx];
           *reinterpret_cast<uint4*>(w + nrow * 64 + ((c ^ ((nrow >> 1) & 3)) << 4)) = unpack16(word);
         }
         fence_proxy_async_smem();
@@ -265,21 +283,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each warp fetches the next unit's step scales one unit ahead (lane l
+    // holds steps l, l+32, ...: a scale, negated for an up-matrix step) and
+    // puts them in its shared-memory row when the unit starts, so no step
+    // waits on the plan or the scale table.
     const int q = warp & 3, half = (warp - 6) >> 2;
+    float* wsc = epi_scales + (warp - 6) * kRowMax;
     int slot = 0;
     uint32_t sphase = 0;
+    // steps 0..63 of a row come one unit ahead in registers; any further steps
+    // (rows of more than 64 live tiles) are fetched when their unit starts
+    constexpr int kAhead = 2;
+    float ahead[kAhead];
+    int cnt_ahead = 0;
+    auto step_scale = [&](int rn, int j) {
+      const uint32_t e = p.plan[size_t(rn) * p.S + j];
+      const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
+      return (k0 != 255u) ? p.scales0[size_t(rn) * p.K0 + k0] : -p.scales1[size_t(rn) * p.K1 + k1];
+    };
+    auto fetch = [&](int u_next) {
+      const int rn = u_next % p.R;
+      cnt_ahead = p.counts[rn] & 0xFFFF;
+#pragma unroll
+      for (int t = 0; t < kAhead; ++t) {
+        const int j = lane + 32 * t;
+        ahead[t] = j < cnt_ahead ? step_scale(rn, j) : 0.f;
+      }
+    };
+    if (int(blockIdx.x) < n_units) fetch(blockIdx.x);
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int m = u / p.R, r = u % p.R;
-      const int n = p.counts[r] & 0xFFFF;
+      const int n = cnt_ahead;
+      __syncwarp();
+#pragma unroll
+      for (int t = 0; t < kAhead; ++t)
+        if (lane + 32 * t < n) wsc[lane + 32 * t] = ahead[t];
+      for (int j = 32 * kAhead + lane; j < n; j += 32) wsc[j] = step_scale(r, j);
+      __syncwarp();
+      if (u + int(gridDim.x) < n_units) fetch(u + gridDim.x);
       float acc0[32], acc1[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) acc0[j] = acc1[j] = 0.f;
       bool alive = true;
       for (int s = 0; s < n; ++s) {
-        const uint32_t e = p.plan[size_t(r) * p.S + s];
-        const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
-        const bool is0 = k0 != 255u;
-        const float sc = is0 ? p.scales0[size_t(r) * p.K0 + k0] : p.scales1[size_t(r) * p.K1 + k1];
+        const float ss = wsc[s];
+        const bool is0 = !GU || ss > 0.f;  // scales are >= 1e-8; up steps were stored negated
+        const float sc = fabsf(ss);
         const bool got = mbar_wait(&tfull[slot], sphase, ctl);
         if (!__all_sync(0xffffffffu, got)) {  // warp-uniform before the collective tcgen05.ld
           alive = false;
