@@ -91,6 +91,22 @@ GU_DRAM_NOTE = {5: "ncu --set full at T=32768, scaled x8 by units",
                 2: "ncu --set full on the full config-2 launch"}
 
 
+def algorithmic_hbm_bytes(cfg, T: int) -> float:
+    """HBM bytes one forward must move (bf16): x read, h written and read
+    back, residual read, out written, weights read once; times L for the loop."""
+    d, F, B = cfg.d_model, cfg.d_ff, cfg.B
+    w = 2.0 * B * B * (2 * (F // B) * cfg.K_gu + (d // B) * cfg.K_d)
+    return (2.0 * T * d + 4.0 * T * F + 2.0 * T * d + 2.0 * T * d + w) * cfg.L
+
+
+def hbm_line(cfg, T, ms, world, hbm_peak, peak_src):
+    if cfg.dtype != "bf16":
+        return None
+    achieved = algorithmic_hbm_bytes(cfg, T) / (ms / 1e3) / 1e9 / world  # per GPU
+    return {"achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "peak_source": f"{peak_src} copy bandwidth", "note": "algorithmic bytes of the whole step per GPU"}
+
+
 def cpu_baseline_sample(cfg, tokens: int, reps: int = 1):
     """Time the oracle (numpy restatement of the reference gather+GEMM path)
     on `tokens` tokens of `cfg` using every host core; returns tokens/s."""
@@ -363,6 +379,7 @@ def run_gpu(args, cfg, rank, world):
                        "parallelism": f"dff{world}" if world > 1 else "single",
                        "L": cfg.L, "l2": l2_note},
             "tflops_effective": tflops, "tflops_effective_per_gpu": tflops / world,
+            "hbm": hbm_line(cfg, T, ms, world, hbm_peak, peak_src),
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(), "e2e": e2e,
         }

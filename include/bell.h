@@ -141,6 +141,12 @@ size_t bell_noalloc_scratch_bytes(int64_t T, int32_t d_ff, int32_t R_gu, int32_t
  * (swiglu_fwd.cu:140-402, launched at :652). */
 int bell_gate_up_bf16(const BellFFNDesc* desc, void* stream);
 
+/* Down half only: out = h Wd (+ residual, or + x when residual is NULL and
+ * add_residual is set), reading the h a bell_gate_up_bf16 call left in
+ * desc->h.  Replaces the reference's second launch,
+ * block_ell_down_residual_kernel (swiglu_fwd.cu:413-559, launched at :690). */
+int bell_down_bf16(const BellFFNDesc* desc, void* stream);
+
 /* One Block-ELL linear (the down projection with residual epilogue, or any
  * block_ell_matmul).  Replaces block_ell_down_residual_kernel
  * (swiglu_fwd.cu:413-559, launched at :690) and the JAX block_ell_matmul

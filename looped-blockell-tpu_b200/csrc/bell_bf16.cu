@@ -655,6 +655,17 @@ int bell_gate_up_bf16(const BellFFNDesc* d, void* stream) {
   return gate_up_bf16(d, status, s);
 }
 
+int bell_down_bf16(const BellFFNDesc* d, void* stream) {
+  if (int rc = check_ffn(d, BELL_DTYPE_BF16)) return rc;
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (int rc = launch_ffn_plan(d, status, s)) return rc;
+  return down_bf16(d, status, s);
+}
+
 int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
   if (d->dtype != BELL_DTYPE_BF16) return fail(BELL_ERR_DTYPE, "bell_linear_bf16: dtype must be BELL_DTYPE_BF16");

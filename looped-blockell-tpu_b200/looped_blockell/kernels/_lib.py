@@ -74,6 +74,7 @@ SIGNATURES = {
     "bell_plan_bytes": (C.c_size_t, [C.c_int32] * 5),
     "bell_swiglu_fwd_bf16": (C.c_int, [C.POINTER(BellFFNDesc), C.c_void_p]),
     "bell_gate_up_bf16": (C.c_int, [C.POINTER(BellFFNDesc), C.c_void_p]),
+    "bell_down_bf16": (C.c_int, [C.POINTER(BellFFNDesc), C.c_void_p]),
     "bell_swiglu_fwd_bf16_noalloc": (C.c_int, [C.POINTER(BellFFNDesc), C.c_void_p]),
     "bell_noalloc_scratch_bytes": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                                 C.c_int32]),

@@ -76,3 +76,29 @@ def test_looped_host_pipeline_equals_device_op():
                             L=3, chunk_tokens=128)
     torch.cuda.synchronize()
     assert torch.equal(out, ref.cpu())
+
+
+def test_gate_up_then_down_equals_fused_entry():
+    """bell_gate_up_bf16 followed by bell_down_bf16 on the same descriptor gives
+    the fused entry's result exactly."""
+    import ctypes as C
+    K = _K()
+    from looped_blockell.kernels import _lib, ops
+    c = make_case(300, 256, 512, 64, 2, 3, 4, seed=31)
+    d = to_dev(c, torch.bfloat16)
+    ref = K.block_ell_swiglu_fwd(d["x"], d["vg"], d["cg"], d["vu"], d["cu"], d["vd"], d["cd"], add_residual=True)
+    lib = _lib.load()
+    x = d["x"].contiguous()
+    h = torch.empty((300, 512), dtype=torch.bfloat16, device="cuda")
+    out = torch.empty_like(x)
+    plan = torch.empty(ops.plan_bytes(8, 2, 3, 4, 4), dtype=torch.uint8, device="cuda")
+    desc = _lib.BellFFNDesc()
+    desc.T, desc.d_model, desc.d_ff, desc.dtype, desc.add_residual = 300, 256, 512, _lib.BELL_DTYPE_BF16, 1
+    desc.x, desc.h, desc.out, desc.plan = x.data_ptr(), h.data_ptr(), out.data_ptr(), plan.data_ptr()
+    desc.gate = ops._ell(d["vg"], d["cg"], 4, 0)
+    desc.up = ops._ell(d["vu"], d["cu"], 4, 0)
+    desc.down = ops._ell(d["vd"], d["cd"], 8, 0)
+    _lib.check(lib.bell_gate_up_bf16(C.byref(desc), ops._stream()), "gate_up")
+    _lib.check(lib.bell_down_bf16(C.byref(desc), ops._stream()), "down")
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
