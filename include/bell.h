@@ -245,6 +245,54 @@ int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const vo
 int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gain, float eps,
                       void* out, void* stream);
 
+/* --------------------------------------------------------------- backward */
+
+/*
+ * The backward of the bf16 SwiGLU (reference titan::block_ell_swiglu_bwd,
+ * csrc/block_ell/block_ell_ops.cpp:83-97, swiglu_bwd.cu:7-35) is built from:
+ *   d_h  = bell_linear_bf16(grad_out, W_down transposed)
+ *   d_g, d_u = bell_silu_mul_bwd_bf16(d_h, gate_pre, up_out)
+ *   d_x  = bell_linear_bf16([d_g | d_u], [W_gate ; W_up] transposed,
+ *                           residual = grad_out)
+ *   d_W  = bell_sddmm_bf16 for each of gate (x, d_g), up (x, d_u) and
+ *          down (h, grad_out).
+ * A transposed Block-ELL holds the same tile bytes, regrouped by column and
+ * read in the other tile layout.
+ */
+
+/* SiLU*up backward (swiglu_bwd.cu:305-334): d_gate = d_h * up * silu'(gate),
+ * d_up = d_h * silu(gate).  d_h, gate_pre, up_out: [T, d_ff] contiguous bf16;
+ * d_gate, d_up: [T, d_ff] bf16 with rows ld_out elements apart (d_ff % 8 == 0,
+ * ld_out % 8 == 0, all pointers 16-byte aligned). */
+int bell_silu_mul_bwd_bf16(int64_t T, int32_t d_ff, const void* d_h, const void* gate_pre, const void* up_out,
+                           void* d_gate, void* d_up, int64_t ld_out, void* stream);
+
+/*
+ * Tile gradients of one Block-ELL weight (sampled dense-dense product):
+ *   grad[r, k] += a[:, c*B:(c+1)*B]^T b[:, r*B:(r+1)*B]  over all T tokens,
+ * c = col_indices[r, k], stored in `layout` ([B_in, B_out] or [B_out, B_in]).
+ * Dead slots (-1) keep a zero tile.  Replaces block_ell_down_backward_dw and
+ * block_ell_proj_backward_dw (swiglu_bwd.cu:13-14, 29-30).  a: [T, C*B],
+ * b: [T, R*B] bf16, rows lda / ldb elements apart (multiples of 8).
+ * grad: [R, K, B, B] fp32, zeroed first unless `accumulate`; grad_bf16
+ * (optional) receives a bf16 copy, as the reference returns.
+ */
+typedef struct BellSddmmDesc {
+  int64_t T;
+  const void* a;
+  const void* b;
+  int64_t lda, ldb;
+  const int32_t* col_indices;  /* [R, K] */
+  int32_t R, C, K, B;
+  int32_t layout;
+  int32_t accumulate;
+  float* grad;
+  void* grad_bf16;             /* optional */
+  int32_t* status;
+} BellSddmmDesc;
+
+int bell_sddmm_bf16(const BellSddmmDesc* desc, void* stream);
+
 /* ---------------------------------------------------------------- L2 pins */
 
 /* Persisting-L2 window over [base, base+bytes) on `stream`; replaces

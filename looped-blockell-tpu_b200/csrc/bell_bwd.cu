@@ -1,0 +1,444 @@
+// bell_bwd.cu — backward pieces of the Block-ELL SwiGLU (bf16).
+//
+// The reference backward (csrc/block_ell/swiglu_bwd.cu:7-35) runs five
+// kernels: d_h = dy W_down, d_W_down, the SiLU*up backward, d_x = d_gate
+// W_gate + d_up W_up (+ dy), d_W_gate / d_W_up.  Here:
+//   * the two transposed products run on the forward linear kernels with a
+//     transposed Block-ELL (same tile bytes read in the flipped layout; built
+//     by the host layer), so they need no kernel of their own;
+//   * bell_silu_mul_bwd_kernel: d_gate = d_h * up * silu'(gate),
+//     d_up = d_h * silu(gate) (swiglu_bwd.cu:305-334);
+//   * bell_sddmm_kernel: the tile gradients d_W[r, k] = a[:, c]^T b[:, r]
+//     summed over tokens (swiglu_bwd.cu:13-14, 29-30), on tcgen05 with the
+//     token dimension as the MMA K: A = a's 128 feature columns of the tile
+//     (two 64-wide groups), B = b's B feature columns, both MN-major straight
+//     from the row-major activations.  Token ranges are split across CTAs
+//     and the fp32 partial tiles are added into the gradient with vector
+//     atomics.  At tile size 64 a work unit covers two slots of one row (the
+//     two 64-feature groups of A come from two column blocks), so M is 128.
+#include <string>
+
+#include "bell_host.h"
+#include "bell_ptx.cuh"
+
+namespace bell {
+namespace bwd {
+
+// dh, g, u: [T, F] contiguous; dg, du: rows `ld` elements apart (so both can
+// be the two halves of one [T, 2F] buffer).  f8 = F / 8; n8 = T * f8.
+__global__ void __launch_bounds__(256) bell_silu_mul_bwd_kernel(const __nv_bfloat16* __restrict__ dh,
+                                                                const __nv_bfloat16* __restrict__ g,
+                                                                const __nv_bfloat16* __restrict__ u,
+                                                                __nv_bfloat16* __restrict__ dg,
+                                                                __nv_bfloat16* __restrict__ du, int64_t n8,
+                                                                int64_t f8, int64_t ld) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint4 vh = ld_global_nc_v4(dh + i * 8), vg = ld_global_nc_v4(g + i * 8), vu = ld_global_nc_v4(u + i * 8);
+    const uint32_t wh[4] = {vh.x, vh.y, vh.z, vh.w}, wg[4] = {vg.x, vg.y, vg.z, vg.w}, wu[4] = {vu.x, vu.y, vu.z, vu.w};
+    uint32_t og[4], ou[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 h2 = unpack_bf16x2(wh[t]), g2 = unpack_bf16x2(wg[t]), u2 = unpack_bf16x2(wu[t]);
+      const float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
+      og[t] = pack_bf16x2(h2.x * u2.x * (s0 + g2.x * s0 * (1.f - s0)), h2.y * u2.y * (s1 + g2.y * s1 * (1.f - s1)));
+      ou[t] = pack_bf16x2(h2.x * g2.x * s0, h2.y * g2.y * s1);
+    }
+    const int64_t row = i / f8, off = row * ld + (i - row * f8) * 8;
+    st_global_v4(dg + off, og[0], og[1], og[2], og[3]);
+    st_global_v4(du + off, ou[0], ou[1], ou[2], ou[3]);
+  }
+}
+
+__global__ void __launch_bounds__(256) bell_f32_to_bf16_kernel(const float* __restrict__ src,
+                                                               __nv_bfloat16* __restrict__ dst, int64_t n8) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const float4 a = *reinterpret_cast<const float4*>(src + i * 8);
+    const float4 b = *reinterpret_cast<const float4*>(src + i * 8 + 4);
+    st_global_v4(dst + i * 8, pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                 pack_bf16x2(b.z, b.w));
+  }
+}
+
+// ------------------------------------------------------------------ SDDMM
+
+static constexpr int kTok = 64;                // tokens per stage (MMA K per stage)
+static constexpr int kABytes = kTok * 128 * 2;  // 16 KB: 64 tokens x 128 features of a
+static constexpr int kNS = 6;
+static constexpr int kThr = 192;  // warp 0 producer, 1 MMA, 2-5 epilogue
+
+template <int B>
+struct SCfg {
+  static constexpr int B_BYTES = kTok * B * 2;  // 8 / 16 KB: 64 tokens x B features of b
+  static constexpr int STAGE = kABytes + B_BYTES;
+  static constexpr int SMEM = kNS * STAGE + 1024 + 512;
+  static constexpr int SLOTS = B == 64 ? 2 : 1;  // slots of one row per unit
+};
+
+struct SddmmParams {
+  int64_t T;
+  int32_t R, K, KP;          // rows, slots per row, slot groups per row (K / SLOTS, rounded up)
+  int32_t C;                 // column blocks of a (a_cols / B)
+  int32_t n_split;           // token ranges
+  int64_t split_chunks;      // 64-token chunks per token range
+  const int32_t* cols;       // [R, K]
+  float* grad;               // [R, K, B, B] fp32, accumulated
+  int32_t out_in;            // tile layout of grad: 0 [B_in, B_out], 1 [B_out, B_in]
+  int32_t* status;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+struct Unit {
+  int r, k0, k1, c0, c1;
+  int64_t ch0, ch1;  // 64-token chunks [ch0, ch1)
+  bool any;
+};
+
+template <int SLOTS>
+__device__ __forceinline__ Unit unit_of(int u, const SddmmParams& p) {
+  Unit x;
+  const int per = p.R * p.KP;
+  const int s = u / per, rem = u - s * per;
+  x.r = rem / p.KP;
+  const int kp = rem - x.r * p.KP;
+  x.k0 = kp * SLOTS;
+  x.k1 = (SLOTS == 2 && x.k0 + 1 < p.K) ? x.k0 + 1 : -1;
+  const int c0 = p.cols[size_t(x.r) * p.K + x.k0];
+  const int c1 = x.k1 >= 0 ? p.cols[size_t(x.r) * p.K + x.k1] : -1;
+  x.c0 = (c0 >= 0 && c0 < p.C) ? c0 : -1;
+  x.c1 = (c1 >= 0 && c1 < p.C) ? c1 : -1;
+  const int64_t total = (p.T + kTok - 1) / kTok;
+  x.ch0 = int64_t(s) * p.split_chunks;
+  x.ch1 = x.ch0 + p.split_chunks < total ? x.ch0 + p.split_chunks : total;
+  x.any = (x.c0 >= 0 || x.c1 >= 0) && x.ch1 > x.ch0;
+  return x;
+}
+
+template <int B>
+__global__ void __launch_bounds__(kThr, 1)
+    bell_sddmm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                      const SddmmParams p) {
+  using C = SCfg<B>;
+  constexpr int SLOTS = C::SLOTS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kNS * C::STAGE);
+  uint64_t* empty = full + kNS;
+  uint64_t* acc_full = empty + kNS;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Ctl ctl{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * B);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_units = p.n_split * p.R * p.KP;
+
+  if (warp == 0) {
+    if (lane == 0) {  // -------------------------------------------- producer
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_b);
+      const uint64_t pol = policy_evict_normal();
+      int stage = 0, last = -1;
+      uint32_t phase = 0, last_phase = 0;
+      bool alive = true;
+      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+        const Unit x = unit_of<SLOTS>(u, p);
+        if (u < p.R * p.KP) {  // first token range: report indices outside [-1, C)
+#pragma unroll
+          for (int j = 0; j < SLOTS; ++j) {
+            const int k = x.k0 + j;
+            if (k < p.K) {
+              const int c = p.cols[size_t(x.r) * p.K + k];
+              if (c < -1 || c >= p.C) atomicOr(p.status, BELL_STATUS_COLIDX);
+            }
+          }
+        }
+        if (!x.any) continue;
+        for (int64_t ch = x.ch0; ch < x.ch1; ++ch) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
+            alive = false;
+            break;
+          }
+          uint8_t* st = smem + stage * C::STAGE;
+          const int y = int(ch * kTok);
+          uint32_t bytes = C::B_BYTES;
+          if (B == 128) bytes += x.c0 >= 0 ? kABytes : 0;
+          else bytes += (x.c0 >= 0 ? kABytes / 2 : 0) + (x.c1 >= 0 ? kABytes / 2 : 0);
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          if (B == 128) {
+            if (x.c0 >= 0) {
+              tma_load_2d(st, &tm_a, &full[stage], x.c0 * 128, y, pol);
+              tma_load_2d(st + 8192, &tm_a, &full[stage], x.c0 * 128 + 64, y, pol);
+            }
+          } else {
+            if (x.c0 >= 0) tma_load_2d(st, &tm_a, &full[stage], x.c0 * 64, y, pol);
+            if (x.c1 >= 0) tma_load_2d(st + 8192, &tm_a, &full[stage], x.c1 * 64, y, pol);
+          }
+#pragma unroll
+          for (int h = 0; h < B / 64; ++h)
+            tma_load_2d(st + kABytes + h * 8192, &tm_b, &full[stage], x.r * B + h * 64, y, pol);
+          last = stage;
+          last_phase = phase;
+          if (++stage == kNS) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!alive && last >= 0) {  // error path: let the copies in flight land
+        int st = last;
+        uint32_t ph = last_phase;
+        for (int i = 0; i < kNS; ++i) {
+          const uint32_t a = smem_u32(&full[st]);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+          if (--st < 0) {
+            st = kNS - 1;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    const bool leader = elect_one();
+    constexpr uint32_t IDESC = idesc_bf16(128, B, true, true);
+    const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 8192, 1024);
+    const uint64_t b_desc0 = sdesc_sw128(smem_u32(smem) + kABytes, 8192, 1024);
+    int stage = 0, i = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const Unit x = unit_of<SLOTS>(u, p);
+      if (!x.any) continue;
+      const int buf = i & 1;
+      const uint32_t use = uint32_t(i >> 1);
+      ++i;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl))) break;
+      tc_fence_after();
+      const uint32_t d = tmem + uint32_t(buf * B);
+      bool ok = true;
+      for (int64_t ch = x.ch0; ch < x.ch1; ++ch) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ctl))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = a_desc0 + uint64_t(stage) * (C::STAGE >> 4);
+        const uint64_t bd = b_desc0 + uint64_t(stage) * (C::STAGE >> 4);
+        if (leader) {
+#pragma unroll
+          for (int kk = 0; kk < kTok / 16; ++kk)
+            mma_bf16(d, ad + kk * (2048 >> 4), bd + kk * (2048 >> 4), IDESC, (ch > x.ch0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == kNS) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (leader) mma_commit(&acc_full[buf]);
+      __syncwarp();
+    }
+    // every MMA has completed before TMEM is released
+    if (leader) {
+      mma_commit(drain);
+      const uint32_t a = smem_u32(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < 100000000ull) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // accumulator row = feature of a
+    int i = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const Unit x = unit_of<SLOTS>(u, p);
+      if (!x.any) continue;
+      const int buf = i & 1;
+      const uint32_t use = uint32_t(i >> 1);
+      ++i;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1u, ctl))) break;
+      tc_fence_after();
+      // the rows of this warp belong to one slot: at B=64 rows 64-127 are the second slot
+      const int k = (B == 64 && q >= 2) ? x.k1 : x.k0;
+      const int c = (B == 64 && q >= 2) ? x.c1 : x.c0;
+      const int trow = B == 64 ? (row & 63) : row;
+      float* tile = p.grad + (size_t(x.r) * p.K + (k >= 0 ? k : 0)) * B * B;
+      const uint32_t tb = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * B);
+#pragma unroll 1
+      for (int j = 0; j < B / 32; ++j) {
+        uint32_t v[32];
+        tmem_ld32_sync(tb + j * 32, v);
+        if (c < 0) continue;
+        if (!p.out_in) {  // [B_in, B_out]: this row's 32 outputs are contiguous
+          float* dst = tile + size_t(trow) * B + j * 32;
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            red_add_v4(dst + 4 * t, __uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                       __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
+        } else {  // [B_out, B_in]: consecutive lanes hit consecutive addresses
+#pragma unroll
+          for (int t = 0; t < 32; ++t) atomicAdd(tile + size_t(j * 32 + t) * B + trow, __uint_as_float(v[t]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * B);
+  }
+}
+
+// ------------------------------------------------------------------- host
+
+namespace {
+
+int grid_for(int64_t n8, int sms) {
+  const int64_t want = (n8 + 255) / 256;
+  const int64_t cap = int64_t(sms) * 8;
+  return int(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+template <int B>
+int launch_sddmm(const BellSddmmDesc* d, int32_t* status, cudaStream_t s, int sms) {
+  using C = SCfg<B>;
+  CUtensorMap ma, mb;
+  if (int rc = make_map_2d(&ma, d->a, MapType::BF16, uint64_t(d->C) * B, uint64_t(d->T), uint64_t(d->lda) * 2, 64,
+                           kTok, Swz::B128))
+    return rc;
+  if (int rc = make_map_2d(&mb, d->b, MapType::BF16, uint64_t(d->R) * B, uint64_t(d->T), uint64_t(d->ldb) * 2, 64,
+                           kTok, Swz::B128))
+    return rc;
+  SddmmParams p{};
+  p.T = d->T;
+  p.R = d->R;
+  p.K = d->K;
+  p.KP = (d->K + C::SLOTS - 1) / C::SLOTS;
+  p.C = d->C;
+  const int64_t chunks = (d->T + kTok - 1) / kTok;
+  const int64_t per = int64_t(p.R) * p.KP;
+  // token ranges: about 4 work units per SM, each range at least 16 chunks
+  // (1024 tokens) so the fp32 tile additions stay small next to the loads
+  int64_t n_split = (int64_t(4) * sms + per - 1) / per;
+  const int64_t max_split = chunks / 16 > 1 ? chunks / 16 : 1;
+  if (n_split > max_split) n_split = max_split;
+  if (n_split < 1) n_split = 1;
+  p.split_chunks = (chunks + n_split - 1) / n_split;
+  p.n_split = int32_t((chunks + p.split_chunks - 1) / p.split_chunks);
+  p.cols = d->col_indices;
+  p.grad = d->grad;
+  p.out_in = d->layout == BELL_TILE_OUT_IN;
+  p.status = status;
+  p.timeout_ns = wait_budget_ns();
+  const int64_t n_units = per * p.n_split;
+  if (n_units > INT32_MAX) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: too many work units");
+  auto kern = bell_sddmm_kernel<B>;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), C::SMEM)) return rc;
+  const int grid = int(n_units < sms ? n_units : sms);
+  kern<<<grid, kThr, C::SMEM, s>>>(ma, mb, p);
+  return check_launch("bell_sddmm_kernel");
+}
+
+}  // namespace
+}  // namespace bwd
+}  // namespace bell
+
+using namespace bell;
+using namespace bell::bwd;
+
+extern "C" {
+
+int bell_silu_mul_bwd_bf16(int64_t T, int32_t d_ff, const void* d_h, const void* gate_pre, const void* up_out,
+                           void* d_gate, void* d_up, int64_t ld_out, void* stream) {
+  if (!d_h || !gate_pre || !up_out || !d_gate || !d_up) return fail(BELL_ERR_ARG, "bell_silu_mul_bwd_bf16: NULL pointer");
+  if (T < 0 || d_ff <= 0 || d_ff % 8 != 0 || ld_out < d_ff || ld_out % 8 != 0)
+    return fail(BELL_ERR_SHAPE, "bell_silu_mul_bwd_bf16: need T >= 0, d_ff % 8 == 0, ld_out >= d_ff, ld_out % 8 == 0");
+  if (!aligned16(d_h) || !aligned16(gate_pre) || !aligned16(up_out) || !aligned16(d_gate) || !aligned16(d_up))
+    return fail(BELL_ERR_ALIGN, "bell_silu_mul_bwd_bf16: pointers must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  if (T == 0) return BELL_OK;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const int64_t f8 = d_ff / 8, n8 = T * f8;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bell_silu_mul_bwd_kernel<<<grid_for(n8, sms), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(d_h), static_cast<const __nv_bfloat16*>(gate_pre),
+      static_cast<const __nv_bfloat16*>(up_out), static_cast<__nv_bfloat16*>(d_gate),
+      static_cast<__nv_bfloat16*>(d_up), n8, f8, ld_out);
+  return check_launch("bell_silu_mul_bwd_kernel");
+}
+
+int bell_sddmm_bf16(const BellSddmmDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "bell_sddmm_bf16: NULL descriptor");
+  if (!d->col_indices || !d->grad || (d->T > 0 && (!d->a || !d->b)))
+    return fail(BELL_ERR_ARG, "bell_sddmm_bf16: NULL pointer");
+  if (d->B != 64 && d->B != 128) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: tile size must be 64 or 128");
+  if (d->T < 0 || d->R <= 0 || d->C <= 0 || d->K <= 0)
+    return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: need T >= 0 and R, C, K > 0");
+  if (d->T > INT32_MAX - 64) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: T too large");
+  if (d->lda < int64_t(d->C) * d->B || d->ldb < int64_t(d->R) * d->B)
+    return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: row pitch smaller than the row");
+  if (d->layout != BELL_TILE_IN_OUT && d->layout != BELL_TILE_OUT_IN)
+    return fail(BELL_ERR_ARG, "bell_sddmm_bf16: unknown tile layout");
+  if (!aligned16(d->grad) || (d->grad_bf16 && !aligned16(d->grad_bf16)))
+    return fail(BELL_ERR_ALIGN, "bell_sddmm_bf16: gradient buffers must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const size_t n = size_t(d->R) * d->K * d->B * d->B;
+  if (!d->accumulate) {
+    cudaError_t e = cudaMemsetAsync(d->grad, 0, n * sizeof(float), s);
+    if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  }
+  if (d->T > 0) {
+    const int rc = d->B == 64 ? launch_sddmm<64>(d, status, s, sms) : launch_sddmm<128>(d, status, s, sms);
+    if (rc) return rc;
+  }
+  if (d->grad_bf16) {
+    const int64_t n8 = int64_t(n / 8);
+    bell_f32_to_bf16_kernel<<<grid_for(n8, sms), 256, 0, s>>>(d->grad, static_cast<__nv_bfloat16*>(d->grad_bf16), n8);
+    return check_launch("bell_f32_to_bf16_kernel");
+  }
+  return BELL_OK;
+}
+
+}  // extern "C"

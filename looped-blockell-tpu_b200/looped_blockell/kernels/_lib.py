@@ -65,6 +65,13 @@ class BellLoopDesc(C.Structure):
                 ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p)]
 
 
+class BellSddmmDesc(C.Structure):
+    _fields_ = [("T", C.c_int64), ("a", C.c_void_p), ("b", C.c_void_p), ("lda", C.c_int64), ("ldb", C.c_int64),
+                ("col_indices", C.c_void_p), ("R", C.c_int32), ("C", C.c_int32), ("K", C.c_int32),
+                ("B", C.c_int32), ("layout", C.c_int32), ("accumulate", C.c_int32), ("grad", C.c_void_p),
+                ("grad_bf16", C.c_void_p), ("status", C.c_void_p)]
+
+
 # every exported symbol of include/bell.h: name -> (restype, argtypes)
 SIGNATURES = {
     "bell_abi_version": (C.c_int, []),
@@ -87,6 +94,9 @@ SIGNATURES = {
                                            C.c_void_p, C.c_void_p]),
     "bell_rmsnorm_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
                                     C.c_void_p]),
+    "bell_silu_mul_bwd_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_int64, C.c_void_p]),
+    "bell_sddmm_bf16": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
     "bell_pin_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "bell_unpin_l2": (C.c_int, [C.c_void_p]),
 }

@@ -12,8 +12,9 @@ Like the reference's native ops, these take ``[B_out, B_in]`` weight tiles
 to the JAX ``[B_in, B_out]`` layout.  The Meta implementation takes d_ff from
 ``v_gate.size(0) * v_gate.size(2)`` (the reference hard-codes a tile size of
 16 there, block_ell_ops.cpp:208).  There is no CPU kernel: CPU tensors fail at
-dispatch, as with the reference extension.  The backward op
-(``block_ell_swiglu_bwd``) is not registered; this build is forward-only.
+dispatch, as with the reference extension.  ``block_ell_swiglu_bwd`` returns
+``(dx, d_v_gate, d_v_up, d_v_down)`` with ``grad_out`` added into ``dx``, as the
+reference op does (swiglu_bwd.cu:785-796).
 """
 
 from __future__ import annotations
@@ -22,6 +23,7 @@ from typing import List
 
 import torch
 
+from . import backward as _bwd
 from . import loop as _loop
 from . import ops as _ops
 
@@ -33,6 +35,9 @@ _SCHEMAS = {
     "block_ell_swiglu_fwd_with_intermediate":
         "block_ell_swiglu_fwd_with_intermediate(Tensor x, Tensor v_gate, Tensor ci_gate, Tensor v_up, "
         "Tensor ci_up, Tensor v_down, Tensor ci_down, bool add_residual) -> (Tensor, Tensor, Tensor, Tensor)",
+    "block_ell_swiglu_bwd": "block_ell_swiglu_bwd(Tensor grad_out, Tensor x, Tensor gate_pre_act, Tensor up_out, "
+                            "Tensor h, Tensor v_gate, Tensor ci_gate, Tensor v_up, Tensor ci_up, Tensor v_down, "
+                            "Tensor ci_down) -> (Tensor, Tensor, Tensor, Tensor)",
     "pin_weights_l2": "pin_weights_l2(Tensor[] weights) -> ()",
     "unpin_weights_l2": "unpin_weights_l2() -> ()",
     "persistent_mlp_step": "persistent_mlp_step(Tensor h, Tensor e, Tensor log_A, Tensor log_dt, "
@@ -59,6 +64,15 @@ def _fwd_int_meta(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual
     d_ff = v_gate.size(0) * v_gate.size(2)
     mid = x.new_empty((x.size(0), d_ff))
     return torch.empty_like(x), mid, torch.empty_like(mid), torch.empty_like(mid)
+
+
+def _bwd_cuda(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, v_up, ci_up, v_down, ci_down):
+    return tuple(_bwd.block_ell_swiglu_bwd(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, v_up, ci_up,
+                                           v_down, ci_down, layout=_ops.TILE_OUT_IN))
+
+
+def _bwd_meta(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, v_up, ci_up, v_down, ci_down):
+    return torch.empty_like(x), torch.empty_like(v_gate), torch.empty_like(v_up), torch.empty_like(v_down)
 
 
 def _pin(weights: List[torch.Tensor]):
@@ -103,6 +117,8 @@ def register() -> bool:
     lib.impl("block_ell_swiglu_fwd", _fwd_meta, "Meta")
     lib.impl("block_ell_swiglu_fwd_with_intermediate", _fwd_int_cuda, "CUDA")
     lib.impl("block_ell_swiglu_fwd_with_intermediate", _fwd_int_meta, "Meta")
+    lib.impl("block_ell_swiglu_bwd", _bwd_cuda, "CUDA")
+    lib.impl("block_ell_swiglu_bwd", _bwd_meta, "Meta")
     lib.impl("pin_weights_l2", _pin, "CompositeExplicitAutograd")
     lib.impl("unpin_weights_l2", _unpin, "CompositeExplicitAutograd")
     lib.impl("persistent_mlp_step", _step_cuda, "CUDA")

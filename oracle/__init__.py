@@ -1,7 +1,8 @@
 """CPU oracle for the Block-ELL SwiGLU hot path — TEST INFRASTRUCTURE ONLY.
 
 This package restates, on the CPU, the reference algorithm of
-bigwolfeman/looped-blockell-tpu for the Block-ELL SwiGLU forward path.
+bigwolfeman/looped-blockell-tpu for the Block-ELL SwiGLU forward path
+and its backward.
 It exists so the CUDA path can be checked against it.  Only the test suite,
 ``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference``
 legs of ``bench.py`` may import it, and only as a checker or as the timed CPU

@@ -28,7 +28,7 @@ LAYOUT_OUT_IN = 1
 __all__ = [
     "LAYOUT_IN_OUT", "LAYOUT_OUT_IN",
     "random_topology", "block_ell_to_dense", "dense_to_block_ell",
-    "block_ell_matmul", "silu", "swiglu_ffn", "rmsnorm", "looped_ffn",
+    "block_ell_matmul", "silu", "swiglu_ffn", "swiglu_ffn_backward", "rmsnorm", "looped_ffn",
     "ternary_quantize_tiles", "activation_quantize_int", "pack_ternary",
     "unpack_ternary", "ternary_block_ell_matmul", "ternary_swiglu_ffn",
     "bf16_round", "rel_l2", "nnz_flops",
@@ -184,6 +184,53 @@ def swiglu_ffn(x, gate, up, down, add_residual=False, residual=None,
     if return_intermediates:
         return out, h, g, u
     return out
+
+
+def _tile_grads(dense_grad: np.ndarray, cols: np.ndarray, B: int, layout: int) -> np.ndarray:
+    """Per-slot tile gradients from a dense ``[out, in]`` gradient: slot (r, k)
+    gets block (r, cols[r, k]) as a [B_in, B_out] tile (zeros for dead slots),
+    returned in the stored ``layout``."""
+    R, K = cols.shape
+    out = np.zeros((R, K, B, B), dtype=np.float64)
+    for r in range(R):
+        for k in range(K):
+            c = int(cols[r, k])
+            if c >= 0:
+                out[r, k] = dense_grad[r * B:(r + 1) * B, c * B:(c + 1) * B].T
+    return out if layout == LAYOUT_IN_OUT else np.swapaxes(out, -1, -2)
+
+
+def swiglu_ffn_backward(x, gate, up, down, dy, add_residual=True):
+    """Gradients of ``out = W_down(silu(W_gate x) * W_up x) (+ x)``.
+
+    The reference's backward (csrc/block_ell/swiglu_bwd.cu:7-35) computes
+    d_h = dy W_down, d_gate = d_h * up * silu'(gate), d_up = d_h * silu(gate)
+    (:305-334), d_x = d_gate W_gate + d_up W_up, plus dy for the residual
+    (:785-796, always added there; ``add_residual`` selects it here), and
+    d_W[r, k] = a[:, c]^T b[:, r] per live tile (:13-14, :29-30).  Restated
+    densely in float64: returns (dx, dv_gate, dv_up, dv_down) with the tile
+    gradients in each matrix's stored layout (dead slots get zeros).
+    """
+    xv = np.asarray(x, dtype=np.float64)
+    dyv = np.asarray(dy, dtype=np.float64)
+    d = xv.shape[1]
+    (vg, cg, lg), (vu, cu, lu), (vd, cd, ld) = gate, up, down
+    B = vg.shape[-1]
+    F = vg.shape[0] * B
+    Wg = block_ell_to_dense(vg, cg, F, d, lg)
+    Wu = block_ell_to_dense(vu, cu, F, d, lu)
+    Wd = block_ell_to_dense(vd, cd, d, F, ld)
+    g, u = xv @ Wg.T, xv @ Wu.T
+    sig = 1.0 / (1.0 + np.exp(-g))
+    h = g * sig * u
+    dh = dyv @ Wd
+    dg = dh * u * (sig + g * sig * (1.0 - sig))
+    du = dh * g * sig
+    dx = dg @ Wg + du @ Wu
+    if add_residual:
+        dx = dx + dyv
+    return (dx, _tile_grads(dg.T @ xv, cg, B, lg), _tile_grads(du.T @ xv, cu, B, lu),
+            _tile_grads(dyv.T @ h, cd, B, ld))
 
 
 def rmsnorm(x: np.ndarray, gain: np.ndarray, eps: float = 1e-5, dtype=np.float64) -> np.ndarray:

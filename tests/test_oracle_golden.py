@@ -117,3 +117,37 @@ def test_random_topology_unique_sorted():
     assert c.shape == (16, 8) and c.dtype == np.int32
     for row in c:
         assert len(np.unique(row)) == 8 and np.all(np.diff(row) > 0)
+
+
+def test_oracle_backward_matches_torch_autograd():
+    """The oracle's SwiGLU gradients equal torch autograd through the dense
+    restatement (float64), including dead and duplicate slots."""
+    import torch
+    rng = np.random.default_rng(7)
+    T, d, F, B = 9, 128, 256, 64
+    cg = np.array([[0, 1], [1, -1], [0, 0], [1, 0]], dtype=np.int32)
+    cu = np.array([[1, 0], [0, 1], [-1, 1], [0, 1]], dtype=np.int32)
+    cd = np.array([[0, 2, 3], [1, 3, -1]], dtype=np.int32)
+    vg = rng.standard_normal((4, 2, B, B)) * 0.05
+    vu = rng.standard_normal((4, 2, B, B)) * 0.05
+    vd = rng.standard_normal((2, 3, B, B)) * 0.05
+    x = rng.standard_normal((T, d))
+    dy = rng.standard_normal((T, d))
+    dx, dvg, dvu, dvd = O.swiglu_ffn_backward(x, (vg, cg, 0), (vu, cu, 0), (vd, cd, 0), dy, add_residual=True)
+    tv = [torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (x, vg, vu, vd)]
+
+    def ell(v, c, out_f, in_f):
+        W = torch.zeros(out_f, in_f, dtype=torch.float64)
+        for r in range(c.shape[0]):
+            for k in range(c.shape[1]):
+                if c[r, k] >= 0:
+                    W = W.index_put((torch.arange(r * B, (r + 1) * B)[:, None],
+                                     torch.arange(c[r, k] * B, (c[r, k] + 1) * B)[None, :]),
+                                    v[r, k].T, accumulate=True)
+        return W
+
+    xt, vgt, vut, vdt = tv
+    out = (torch.nn.functional.silu(xt @ ell(vgt, cg, F, d).T) * (xt @ ell(vut, cu, F, d).T)) @ ell(vdt, cd, d, F).T + xt
+    out.backward(torch.tensor(dy))
+    for mine, ref in ((dx, xt.grad), (dvg, vgt.grad), (dvu, vut.grad), (dvd, vdt.grad)):
+        np.testing.assert_allclose(mine, ref.numpy(), rtol=1e-10, atol=1e-12)
