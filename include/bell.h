@@ -250,8 +250,9 @@ int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gai
 /*
  * The backward of the bf16 SwiGLU (reference titan::block_ell_swiglu_bwd,
  * csrc/block_ell/block_ell_ops.cpp:83-97, swiglu_bwd.cu:7-35) is built from:
- *   d_h  = bell_linear_bf16(grad_out, W_down transposed)
- *   d_g, d_u = bell_silu_mul_bwd_bf16(d_h, gate_pre, up_out)
+ *   [d_g | d_u] = bell_down_silu_bwd_bf16(grad_out, W_down transposed,
+ *                 gate_pre, up_out)  (or bell_linear_bf16 for d_h followed
+ *                 by bell_silu_mul_bwd_bf16)
  *   d_x  = bell_linear_bf16([d_g | d_u], [W_gate ; W_up] transposed,
  *                           residual = grad_out)
  *   d_W  = bell_sddmm_bf16 for each of gate (x, d_g), up (x, d_u) and
@@ -266,6 +267,29 @@ int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gai
  * ld_out % 8 == 0, all pointers 16-byte aligned). */
 int bell_silu_mul_bwd_bf16(int64_t T, int32_t d_ff, const void* d_h, const void* gate_pre, const void* up_out,
                            void* d_gate, void* d_up, int64_t ld_out, void* stream);
+
+/*
+ * d_h = grad_out @ W_down fused with the SiLU*up backward: the linear
+ * kernel's epilogue turns each fp32 d_h tile into d_gate and d_up, so d_h
+ * never reaches memory (replaces the reference's d_h product and
+ * silu_mul_backward, swiglu_bwd.cu:7-12, 305-334).  w_t is the transposed
+ * down weight (R = d_ff / B block-rows over C = d_model / B column blocks).
+ * grad_out: [T, d_model]; gate_pre, up_out: [T, d_ff]; d_gate_up: [T, 2 d_ff]
+ * with d_gate in columns [0, d_ff) and d_up in [d_ff, 2 d_ff); all bf16.
+ * plan: bell_plan_bytes(0, 0, 0, w_t.R, w_t.K) bytes.
+ */
+typedef struct BellDownBwdDesc {
+  int64_t T;
+  const void* grad_out;
+  const void* gate_pre;
+  const void* up_out;
+  void* d_gate_up;
+  void* plan;
+  BellEll w_t;
+  int32_t* status;
+} BellDownBwdDesc;
+
+int bell_down_silu_bwd_bf16(const BellDownBwdDesc* desc, void* stream);
 
 /*
  * Tile gradients of one Block-ELL weight (sampled dense-dense product):

@@ -27,11 +27,11 @@ namespace bell {
 
 // Token-major gate/up or linear kernel: one phase of the engine
 // (bell_engine.cuh) over all units.
-template <int B, bool GU, bool W_MN>
+template <int B, bool GU, bool W_MN, bool SB = false>
 __global__ void __launch_bounds__(eng::kThreads, 1)
     bell_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w0,
                      const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
-  using G = eng::Geo<B, GU>;
+  using G = eng::Geo<B, GU, SB>;
   extern __shared__ uint8_t smem_raw[];
   const eng::Smem s = eng::carve<G>(smem_raw);
   const uint32_t tmem = eng::setup<G>(s);
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
       break;
     }
     case eng::kEpilogue:
-      eng::epilogue<B, GU, G>(p, s, tmem, 0, ctl);
+      eng::epilogue<B, GU, G, SB>(p, s, tmem, 0, ctl);
       break;
   }
   eng::teardown<G>(tmem);
@@ -485,13 +485,13 @@ static int unit_band(bool gate_up, int R) {
   return band < 1 ? 1 : (band > R ? R : band);
 }
 
-template <int B, bool GU, bool W_MN>
+template <int B, bool GU, bool W_MN, bool SB = false>
 static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1, const Bf16Params& p0,
                        cudaStream_t stream) {
-  using G = eng::Geo<B, GU>;
+  using G = eng::Geo<B, GU, SB>;
   Bf16Params p = p0;
   p.band = unit_band(GU, p.R);
-  auto kern = bell_bf16_kernel<B, GU, W_MN>;
+  auto kern = bell_bf16_kernel<B, GU, W_MN, SB>;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), G::SMEM_BYTES)) return rc;
   int sms = 0;
   if (int rc = device_sm_count(&sms)) return rc;
@@ -706,6 +706,52 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   p.status = status;
   p.timeout_ns = wait_budget_ns();
   return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
+}
+
+int bell_down_silu_bwd_bf16(const BellDownBwdDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (int rc = check_ell(d->w_t, "w_t")) return rc;
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (d->T > 0 && (!d->grad_out || !d->gate_pre || !d->up_out || !d->d_gate_up || !d->plan))
+    return fail(BELL_ERR_ARG, "grad_out, gate_pre, up_out, d_gate_up and plan must be non-NULL");
+  if (!aligned16(d->grad_out) || !aligned16(d->gate_pre) || !aligned16(d->up_out) || !aligned16(d->d_gate_up) ||
+      !aligned16(d->plan))
+    return fail(BELL_ERR_ALIGN, "bell_down_silu_bwd_bf16: pointers must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  const BellEll& w = d->w_t;
+  if (int rc = launch_plan(nullptr, 0, nullptr, 0, 0, 0, w.col_indices, w.K, w.R, w.C, d->plan, status, s)) return rc;
+  const int64_t in_f = int64_t(w.C) * w.B, F = int64_t(w.R) * w.B;
+  CUtensorMap ma, mw;
+  if (int rc = make_map_2d(&ma, d->grad_out, MapType::BF16, in_f, d->T, uint64_t(in_f) * 2, 64, kBM, Swz::B128))
+    return rc;
+  if (int rc = make_w_map(&mw, w)) return rc;
+  PlanLayout L = plan_layout(0, 0, 0, w.R, w.K);
+  Bf16Params p{};
+  p.T = d->T;
+  p.n_mtiles = int32_t((d->T + kBM - 1) / kBM);
+  p.R = w.R;
+  p.K0 = w.K;
+  p.S = w.K;
+  p.plan = reinterpret_cast<const uint32_t*>(static_cast<const char*>(d->plan) + L.d_entries);
+  p.counts = reinterpret_cast<const int32_t*>(static_cast<const char*>(d->plan) + L.d_counts);
+  p.out = d->d_gate_up;
+  p.ld_out = 2 * F;
+  p.bwd_gate = d->gate_pre;
+  p.bwd_up = d->up_out;
+  p.ld_bwd = F;
+  p.du_off = F;
+  p.status = status;
+  p.timeout_ns = wait_budget_ns();
+  // token-major engine at both tile sizes: its epilogue owns whole token
+  // rows, so the gate/up rows are staged with 16-byte copies
+  const bool mn = w.layout == BELL_TILE_IN_OUT;
+  if (w.B == 64)
+    return mn ? launch_bf16<64, false, true, true>(ma, mw, mw, p, s) : launch_bf16<64, false, false, true>(ma, mw, mw, p, s);
+  return mn ? launch_bf16<128, false, true, true>(ma, mw, mw, p, s) : launch_bf16<128, false, false, true>(ma, mw, mw, p, s);
 }
 
 }  // extern "C"

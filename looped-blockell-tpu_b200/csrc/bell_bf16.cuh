@@ -7,6 +7,8 @@
 
 #include <cstdint>
 
+#include "bell_ptx.cuh"
+
 namespace bell {
 
 static constexpr int kBM = 128;        // tokens per tile (MMA M) in the token-major kernels
@@ -31,9 +33,27 @@ struct Bf16Params {
   int32_t out_f32;   // linear: write fp32 instead of bf16
   int32_t band;      // block-rows per band of the unit order (see unit_mr)
   int32_t split;     // feature-major gate/up: one weight tile per plan step
+  // linear with the SiLU*up backward in the epilogue (bwd_gate != NULL): the
+  // accumulator is d_h; reads gate_pre / up_out [T, ld_bwd] bf16 at the same
+  // feature, writes d_gate at out[t, f] and d_up at out[t, du_off + f]
+  const void* bwd_gate;
+  const void* bwd_up;
+  int64_t ld_bwd;
+  int64_t du_off;
   int32_t* status;
   uint64_t timeout_ns;
 };
+
+// d_gate, d_up of h = silu(g) * u for an incoming d_h (the reference
+// swiglu_bwd.cu:305-334 formula), fp32.  sigmoid(g) = 0.5 + 0.5 tanh(g / 2)
+// on the hardware tanh (absolute error below 2^-11 on s, under the bf16
+// rounding of the results); an IEEE reciprocal here made the fused backward
+// epilogue the bottleneck of its kernel.
+__device__ __forceinline__ void silu_mul_grad(float dh, float g, float u, float& dg, float& du) {
+  const float s = fmaf(0.5f, tanh_approx(0.5f * g), 0.5f);
+  dg = dh * u * (s + g * s * (1.f - s));
+  du = dh * g * s;
+}
 
 // Work-unit order: bands of `band` output block-rows; inside a band, all
 // token tiles, block-row fastest.  Consecutive units share a token tile (its

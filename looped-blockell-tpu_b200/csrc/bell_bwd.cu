@@ -18,6 +18,7 @@
 //     two 64-feature groups of A come from two column blocks), so M is 128.
 #include <string>
 
+#include "bell_bf16.cuh"
 #include "bell_host.h"
 #include "bell_ptx.cuh"
 
@@ -39,9 +40,11 @@ __global__ void __launch_bounds__(256) bell_silu_mul_bwd_kernel(const __nv_bfloa
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const float2 h2 = unpack_bf16x2(wh[t]), g2 = unpack_bf16x2(wg[t]), u2 = unpack_bf16x2(wu[t]);
-      const float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
-      og[t] = pack_bf16x2(h2.x * u2.x * (s0 + g2.x * s0 * (1.f - s0)), h2.y * u2.y * (s1 + g2.y * s1 * (1.f - s1)));
-      ou[t] = pack_bf16x2(h2.x * g2.x * s0, h2.y * g2.y * s1);
+      float dg0, du0, dg1, du1;
+      silu_mul_grad(h2.x, g2.x, u2.x, dg0, du0);
+      silu_mul_grad(h2.y, g2.y, u2.y, dg1, du1);
+      og[t] = pack_bf16x2(dg0, dg1);
+      ou[t] = pack_bf16x2(du0, du1);
     }
     const int64_t row = i / f8, off = row * ld + (i - row * f8) * 8;
     st_global_v4(dg + off, og[0], og[1], og[2], og[3]);
@@ -63,14 +66,14 @@ __global__ void __launch_bounds__(256) bell_f32_to_bf16_kernel(const float* __re
 
 static constexpr int kTok = 64;                // tokens per stage (MMA K per stage)
 static constexpr int kABytes = kTok * 128 * 2;  // 16 KB: 64 tokens x 128 features of a
-static constexpr int kNS = 6;
 static constexpr int kThr = 192;  // warp 0 producer, 1 MMA, 2-5 epilogue
 
 template <int B>
 struct SCfg {
   static constexpr int B_BYTES = kTok * B * 2;  // 8 / 16 KB: 64 tokens x B features of b
   static constexpr int STAGE = kABytes + B_BYTES;
-  static constexpr int SMEM = kNS * STAGE + 1024 + 512;
+  static constexpr int NS = 196608 / STAGE;     // 8 / 6 stages
+  static constexpr int SMEM = NS * STAGE + 1024 + 512;
   static constexpr int SLOTS = B == 64 ? 2 : 1;  // slots of one row per unit
 };
 
@@ -117,6 +120,51 @@ __device__ __forceinline__ Unit unit_of(int u, const SddmmParams& p) {
   return x;
 }
 
+// Work split.  Token ranges (splits) run one after another; inside a split
+// the units x chunks of the range are cut into equal contiguous shares, one
+// per CTA, so every CTA streams the same tokens at the same time (the
+// activation tiles are shared through L2) and no CTA waits on a longer share.
+// A share may start or end inside a unit: each piece (segment) adds its
+// partial tiles into the gradient like a whole unit.
+struct SegIt {
+  int s;
+  int64_t L, L1, Ws;
+};
+
+__device__ __forceinline__ void seg_share(const SddmmParams& p, SegIt& it) {
+  it.L = it.Ws * blockIdx.x / gridDim.x;
+  it.L1 = it.Ws * (blockIdx.x + 1) / gridDim.x;
+}
+
+__device__ __forceinline__ SegIt seg_begin(const SddmmParams& p) {
+  SegIt it;
+  it.s = 0;
+  it.Ws = int64_t(p.R) * p.KP * p.split_chunks;
+  seg_share(p, it);
+  return it;
+}
+
+// Next segment of this CTA: unit `x`, chunks [a0, a1) (empty when a1 <= a0),
+// `head` when it starts at the unit's first chunk of split 0.  False at the end.
+template <int SLOTS>
+__device__ __forceinline__ bool seg_next(const SddmmParams& p, SegIt& it, Unit& x, int64_t& a0, int64_t& a1,
+                                         bool& head) {
+  while (it.L >= it.L1) {
+    if (++it.s >= p.n_split) return false;
+    seg_share(p, it);
+  }
+  const int ul = int(it.L / p.split_chunks);
+  const int64_t c_lo = it.L - int64_t(ul) * p.split_chunks;
+  const int64_t end = min(it.L1, int64_t(ul + 1) * p.split_chunks);
+  const int64_t c_hi = end - int64_t(ul) * p.split_chunks;
+  it.L = end;
+  x = unit_of<SLOTS>(it.s * p.R * p.KP + ul, p);
+  a0 = x.ch0 + c_lo;
+  a1 = min(x.ch0 + c_hi, x.ch1);
+  head = it.s == 0 && c_lo == 0;
+  return true;
+}
+
 template <int B>
 __global__ void __launch_bounds__(kThr, 1)
     bell_sddmm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -125,9 +173,9 @@ __global__ void __launch_bounds__(kThr, 1)
   constexpr int SLOTS = C::SLOTS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kNS * C::STAGE);
-  uint64_t* empty = full + kNS;
-  uint64_t* acc_full = empty + kNS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE);
+  uint64_t* empty = full + C::NS;
+  uint64_t* acc_full = empty + C::NS;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -136,7 +184,7 @@ __global__ void __launch_bounds__(kThr, 1)
   Ctl ctl{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kNS; ++s) {
+    for (int s = 0; s < C::NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -156,7 +204,6 @@ __global__ void __launch_bounds__(kThr, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_units = p.n_split * p.R * p.KP;
 
   if (warp == 0) {
     if (lane == 0) {  // -------------------------------------------- producer
@@ -166,9 +213,12 @@ __global__ void __launch_bounds__(kThr, 1)
       int stage = 0, last = -1;
       uint32_t phase = 0, last_phase = 0;
       bool alive = true;
-      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
-        const Unit x = unit_of<SLOTS>(u, p);
-        if (u < p.R * p.KP) {  // first token range: report indices outside [-1, C)
+      SegIt it = seg_begin(p);
+      Unit x;
+      int64_t a0, a1;
+      bool head;
+      while (alive && seg_next<SLOTS>(p, it, x, a0, a1, head)) {
+        if (head) {  // once per unit: report indices outside [-1, C)
 #pragma unroll
           for (int j = 0; j < SLOTS; ++j) {
             const int k = x.k0 + j;
@@ -178,8 +228,8 @@ __global__ void __launch_bounds__(kThr, 1)
             }
           }
         }
-        if (!x.any) continue;
-        for (int64_t ch = x.ch0; ch < x.ch1; ++ch) {
+        if (!x.any || a1 <= a0) continue;
+        for (int64_t ch = a0; ch < a1; ++ch) {
           if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
             alive = false;
             break;
@@ -204,7 +254,7 @@ __global__ void __launch_bounds__(kThr, 1)
             tma_load_2d(st + kABytes + h * 8192, &tm_b, &full[stage], x.r * B + h * 64, y, pol);
           last = stage;
           last_phase = phase;
-          if (++stage == kNS) {
+          if (++stage == C::NS) {
             stage = 0;
             phase ^= 1;
           }
@@ -213,13 +263,13 @@ __global__ void __launch_bounds__(kThr, 1)
       if (!alive && last >= 0) {  // error path: let the copies in flight land
         int st = last;
         uint32_t ph = last_phase;
-        for (int i = 0; i < kNS; ++i) {
+        for (int i = 0; i < C::NS; ++i) {
           const uint32_t a = smem_u32(&full[st]);
           const uint64_t t0 = globaltimer_ns();
           while (!mbar_try_wait(a, ph) && globaltimer_ns() - t0 < 100000000ull) {
           }
           if (--st < 0) {
-            st = kNS - 1;
+            st = C::NS - 1;
             ph ^= 1;
           }
         }
@@ -233,9 +283,12 @@ __global__ void __launch_bounds__(kThr, 1)
     const uint64_t b_desc0 = sdesc_sw128(smem_u32(smem) + kABytes, 8192, 1024);
     int stage = 0, i = 0;
     uint32_t phase = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const Unit x = unit_of<SLOTS>(u, p);
-      if (!x.any) continue;
+    SegIt it = seg_begin(p);
+    Unit x;
+    int64_t a0, a1;
+    bool head;
+    while (seg_next<SLOTS>(p, it, x, a0, a1, head)) {
+      if (!x.any || a1 <= a0) continue;
       const int buf = i & 1;
       const uint32_t use = uint32_t(i >> 1);
       ++i;
@@ -243,7 +296,7 @@ __global__ void __launch_bounds__(kThr, 1)
       tc_fence_after();
       const uint32_t d = tmem + uint32_t(buf * B);
       bool ok = true;
-      for (int64_t ch = x.ch0; ch < x.ch1; ++ch) {
+      for (int64_t ch = a0; ch < a1; ++ch) {
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ctl))) {
           ok = false;
           break;
@@ -254,11 +307,11 @@ __global__ void __launch_bounds__(kThr, 1)
         if (leader) {
 #pragma unroll
           for (int kk = 0; kk < kTok / 16; ++kk)
-            mma_bf16(d, ad + kk * (2048 >> 4), bd + kk * (2048 >> 4), IDESC, (ch > x.ch0 || kk > 0) ? 1u : 0u);
+            mma_bf16(d, ad + kk * (2048 >> 4), bd + kk * (2048 >> 4), IDESC, (ch > a0 || kk > 0) ? 1u : 0u);
           mma_commit(&empty[stage]);
         }
         __syncwarp();
-        if (++stage == kNS) {
+        if (++stage == C::NS) {
           stage = 0;
           phase ^= 1;
         }
@@ -281,9 +334,12 @@ __global__ void __launch_bounds__(kThr, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;  // accumulator row = feature of a
     int i = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const Unit x = unit_of<SLOTS>(u, p);
-      if (!x.any) continue;
+    SegIt it = seg_begin(p);
+    Unit x;
+    int64_t a0, a1;
+    bool head;
+    while (seg_next<SLOTS>(p, it, x, a0, a1, head)) {
+      if (!x.any || a1 <= a0) continue;
       const int buf = i & 1;
       const uint32_t use = uint32_t(i >> 1);
       ++i;
@@ -353,24 +409,22 @@ int launch_sddmm(const BellSddmmDesc* d, int32_t* status, cudaStream_t s, int sm
   p.C = d->C;
   const int64_t chunks = (d->T + kTok - 1) / kTok;
   const int64_t per = int64_t(p.R) * p.KP;
-  // token ranges: about 4 work units per SM, each range at least 16 chunks
-  // (1024 tokens) so the fp32 tile additions stay small next to the loads
-  int64_t n_split = (int64_t(4) * sms + per - 1) / per;
-  const int64_t max_split = chunks / 16 > 1 ? chunks / 16 : 1;
-  if (n_split > max_split) n_split = max_split;
-  if (n_split < 1) n_split = 1;
-  p.split_chunks = (chunks + n_split - 1) / n_split;
+  // token ranges of 4096 tokens: the activations of one range stay in L2
+  // while every unit passes over them; each CTA's share of a range adds a
+  // few partial tiles, small next to its loads
+  const int64_t range = 64;
+  p.split_chunks = chunks < range ? chunks : range;
   p.n_split = int32_t((chunks + p.split_chunks - 1) / p.split_chunks);
   p.cols = d->col_indices;
   p.grad = d->grad;
   p.out_in = d->layout == BELL_TILE_OUT_IN;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
-  const int64_t n_units = per * p.n_split;
-  if (n_units > INT32_MAX) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: too many work units");
+  if (per * p.n_split > INT32_MAX) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: too many work units");
   auto kern = bell_sddmm_kernel<B>;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), C::SMEM)) return rc;
-  const int grid = int(n_units < sms ? n_units : sms);
+  const int64_t share = per * p.split_chunks;  // chunk-steps of one range
+  const int grid = int(share < sms ? share : sms);
   kern<<<grid, kThr, C::SMEM, s>>>(ma, mb, p);
   return check_launch("bell_sddmm_kernel");
 }

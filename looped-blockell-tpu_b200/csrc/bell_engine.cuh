@@ -37,19 +37,32 @@ static constexpr int kThreads = 32 * (kMma1 + 1);  // 10 warps
 
 // Ring and accumulator geometry for tile size B; GU sizes a stage for two
 // weight tiles and an accumulator for gate | up.
-template <int B, bool GU>
+// SB (linear with the SiLU*up backward epilogue) reserves EPI_BYTES for the
+// epilogue's gate/up staging: per epilogue warp, EPI_NSLOT slots of 32 rows x
+// B features of gate and of up — two at B = 64 (this unit's and the next
+// one's copy in flight), one at B = 128 (copied during the accumulator wait),
+// so that the stage ring keeps NR >= 2.
+template <int B, bool GU, bool SB = false>
 struct Geo {
   static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
   static constexpr int W_BYTES = kBK * B * 2;    // 8 / 16 KB
   static constexpr int STAGE_BYTES = A_BYTES + W_BYTES * (GU ? 2 : 1);
-  static constexpr int NS = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
+  static constexpr int EPI_SLOT = SB ? 32 * B * 2 * 2 : 0;  // one warp, one unit: gate | up rows
+  static constexpr int EPI_NSLOT = B == 64 ? 2 : 1;
+  static constexpr int EPI_BYTES = 4 * EPI_NSLOT * EPI_SLOT;
+  static constexpr int NS_FIT = ((196608 - EPI_BYTES) / STAGE_BYTES) & ~1;
+  static constexpr int NS = NS_FIT < 8 ? NS_FIT : 8;
   static constexpr int NR = NS / 2;              // stages per ring
   static constexpr int ACC_COLS = GU ? 2 * B : B;  // fp32 columns of one accumulator
   // two issuers, each double buffered when the four accumulators fit
   static constexpr int NBUF = 4 * ACC_COLS <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = 2 * NBUF * ACC_COLS < 128 ? 128 : 2 * NBUF * ACC_COLS;
   // align + barriers (512) + stage info (64) + one staged plan row per producer
-  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + kProds * kRowMax * 4;
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + kProds * kRowMax * 4 + EPI_BYTES;
+  // the two producers of a ring take alternate steps; with one stage per
+  // ring a producer could wait on a phase two ahead of the stage (parity
+  // aliasing), so each ring needs at least two stages
+  static_assert(NR >= 2, "stage ring");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
   static_assert(NS % 2 == 0, "the stage ring is split between two MMA issuers");
 };
@@ -63,6 +76,7 @@ struct Smem {
   volatile int* abort_flag;
   uint32_t* stage_info;            // [ring * NR + stage]
   uint32_t* rows;                  // [producer][kRowMax]
+  uint8_t* epi;                    // SB: [epilogue warp][slot][gate | up rows], 16-byte aligned
 };
 
 template <class G>
@@ -79,6 +93,7 @@ __device__ __forceinline__ Smem carve(uint8_t* smem_raw) {
   s.abort_flag = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
   s.stage_info = reinterpret_cast<uint32_t*>(ctl + 512);
   s.rows = reinterpret_cast<uint32_t*>(ctl + 576);
+  s.epi = ctl + 576 + kProds * kRowMax * 4;
   return s;
 }
 
@@ -334,8 +349,30 @@ __device__ __forceinline__ void issuer_drain(const Smem& s, int k, bool leader) 
 // bf16 copies of gate/up); linear: out = acc (+ residual), bf16 or fp32.
 // `residual` may alias `out` (each element is read, then written, by the same
 // thread).
-template <int B, bool GU, class G>
+// SB: copy this lane's row of gate_pre and up_out for unit (m, r) — B
+// features each — into slot `slot` of the warp's staging area.  Layout per
+// slot: gate rows [32][B*2 bytes] then up rows; 16-byte chunk c of a row sits
+// at position c ^ (lane & 7), so the lane-per-row reads hit distinct banks.
+template <int B, class G>
+__device__ __forceinline__ void stage_gate_up(const Bf16Params& p, const Smem& s, int m, int r, int q, int lane,
+                                              int slot) {
+  const int64_t row = int64_t(m) * kBM + q * 32 + lane;
+  if (row >= p.T) return;
+  uint8_t* dst = s.epi + (q * G::EPI_NSLOT + slot) * G::EPI_SLOT + lane * (B * 2);
+  const char* g = static_cast<const char*>(p.bwd_gate) + (row * p.ld_bwd + int64_t(r) * B) * 2;
+  const char* u = static_cast<const char*>(p.bwd_up) + (row * p.ld_bwd + int64_t(r) * B) * 2;
+#pragma unroll
+  for (int c = 0; c < B / 8; ++c) {
+    const int pos = c ^ (lane & 7);
+    cp_async16(dst + pos * 16, g + c * 16);
+    cp_async16(dst + 32 * B * 2 + pos * 16, u + c * 16);
+  }
+}
+
+// SB: the linear's epilogue applies the SiLU*up backward (p.bwd_gate).
+template <int B, bool GU, class G, bool SB = false>
 __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int i_base, const Ctl& ctl) {
+  static_assert(!(GU && SB), "the SiLU*up backward epilogue is a linear mode");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
   const int nl = local_units(p.n_mtiles * p.R);
@@ -359,13 +396,41 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
     const int buf = G::NBUF == 2 ? (ik & 1) : 0;
     const uint32_t use = G::NBUF == 2 ? uint32_t(ik >> 1) : uint32_t(ik);
     const int ab = k * 2 + buf;
+    const int64_t row = int64_t(m) * kBM + q * 32 + lane;
+    const bool row_ok = row < p.T;
+    // SiLU*up backward: this unit's gate/up rows were copied to shared memory
+    // (cp.async, one slot per unit) while the previous unit ran; start the
+    // next unit's copy, then wait for this one's (per-thread groups)
+    const bool sb = SB && row_ok;
+    const uint8_t* gu_row = nullptr;
+    if constexpr (SB) {
+      if constexpr (G::EPI_NSLOT == 2) {
+        if (i == 0) {
+          stage_gate_up<B, G>(p, s, m, r, q, lane, 0);
+          cp_async_commit();
+        }
+        if (i + 1 < nl) {
+          int m2, r2;
+          unit_mr(blockIdx.x + (i + 1) * gridDim.x, p, m2, r2);
+          stage_gate_up<B, G>(p, s, m2, r2, q, lane, (i + 1) & 1);
+        }
+        cp_async_commit();
+        cp_async_wait_group<1>();
+      } else {  // one slot: this unit's copy overlaps the accumulator wait
+        stage_gate_up<B, G>(p, s, m, r, q, lane, 0);
+        cp_async_commit();
+      }
+      gu_row = s.epi + (q * G::EPI_NSLOT + (G::EPI_NSLOT == 2 ? (i & 1) : 0)) * G::EPI_SLOT + lane * (B * 2);
+    }
     // warp-uniform before the collective tcgen05.ld
-    if (!__all_sync(0xffffffffu, mbar_wait(&s.acc_full[ab], use & 1u, ctl))) return false;
+    if (!__all_sync(0xffffffffu, mbar_wait(&s.acc_full[ab], use & 1u, ctl))) {
+      if constexpr (SB) cp_async_wait_group<0>();  // no copy into shared memory outlives the CTA
+      return false;
+    }
     tc_fence_after();
     const bool any0 = (cw >> 16) & 1;
     const bool any1 = (cw >> 17) & 1;
-    const int64_t row = int64_t(m) * kBM + q * 32 + lane;
-    const bool row_ok = row < p.T;
+    if constexpr (SB && G::EPI_NSLOT == 1) cp_async_wait_group<0>();
     const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t((k * G::NBUF + buf) * G::ACC_COLS);
 #pragma unroll 1
     for (int j = 0; j < B / 32; ++j) {
@@ -416,7 +481,29 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
         float f[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) f[t] = any0 ? __uint_as_float(a[t]) : 0.f;
-        if (row_ok) {
+        if (sb) {  // SiLU*up backward: f = d_h; gate/up from this lane's staged row
+          const int64_t col = int64_t(r) * B + j * 32;
+          __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out + col;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int c = (j * 4 + t) ^ (lane & 7);  // swizzled 16-byte chunk
+            const uint4 gv = *reinterpret_cast<const uint4*>(gu_row + c * 16);
+            const uint4 uv = *reinterpret_cast<const uint4*>(gu_row + 32 * B * 2 + c * 16);
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+            uint32_t og[4], ou[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const float2 g2 = unpack_bf16x2(gw[w]), u2 = unpack_bf16x2(uw[w]);
+              float dg0, du0, dg1, du1;
+              silu_mul_grad(f[8 * t + 2 * w], g2.x, u2.x, dg0, du0);
+              silu_mul_grad(f[8 * t + 2 * w + 1], g2.y, u2.y, dg1, du1);
+              og[w] = pack_bf16x2(dg0, dg1);
+              ou[w] = pack_bf16x2(du0, du1);
+            }
+            st_global_v4(orow + t * 8, og[0], og[1], og[2], og[3]);
+            st_global_v4(orow + p.du_off + t * 8, ou[0], ou[1], ou[2], ou[3]);
+          }
+        } else if (row_ok) {
           const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
           if (p.add_residual) {
             const __nv_bfloat16* rrow = static_cast<const __nv_bfloat16*>(p.residual) + off;

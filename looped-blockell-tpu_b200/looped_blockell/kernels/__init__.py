@@ -11,8 +11,8 @@ from .ops import (TILE_IN_OUT, TILE_OUT_IN, block_ell_linear, block_ell_swiglu_f
                   block_ell_swiglu_fwd_with_intermediate, plan_bytes, read_status, rmsnorm)
 from .loop import (diagonal_injection, looped_ffn, persistent_mlp_step, pin_weights_l2,  # noqa: F401
                    unpin_weights_l2)
-from .backward import (block_ell_sddmm, block_ell_swiglu, block_ell_swiglu_bwd, silu_mul_bwd,  # noqa: F401
-                       transpose_ell, transposed_topology)
+from .backward import (block_ell_sddmm, block_ell_swiglu, block_ell_swiglu_bwd, down_silu_bwd,  # noqa: F401
+                       silu_mul_bwd, transpose_ell, transposed_topology)
 from .stream import block_ell_swiglu_fwd_host, looped_ffn_host, pipeline_tokens  # noqa: F401
 from . import torch_ops as _torch_ops
 

@@ -65,6 +65,11 @@ class BellLoopDesc(C.Structure):
                 ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p)]
 
 
+class BellDownBwdDesc(C.Structure):
+    _fields_ = [("T", C.c_int64), ("grad_out", C.c_void_p), ("gate_pre", C.c_void_p), ("up_out", C.c_void_p),
+                ("d_gate_up", C.c_void_p), ("plan", C.c_void_p), ("w_t", BellEll), ("status", C.c_void_p)]
+
+
 class BellSddmmDesc(C.Structure):
     _fields_ = [("T", C.c_int64), ("a", C.c_void_p), ("b", C.c_void_p), ("lda", C.c_int64), ("ldb", C.c_int64),
                 ("col_indices", C.c_void_p), ("R", C.c_int32), ("C", C.c_int32), ("K", C.c_int32),
@@ -96,6 +101,7 @@ SIGNATURES = {
                                     C.c_void_p]),
     "bell_silu_mul_bwd_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_int64, C.c_void_p]),
+    "bell_down_silu_bwd_bf16": (C.c_int, [C.POINTER(BellDownBwdDesc), C.c_void_p]),
     "bell_sddmm_bf16": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
     "bell_pin_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "bell_unpin_l2": (C.c_int, [C.c_void_p]),

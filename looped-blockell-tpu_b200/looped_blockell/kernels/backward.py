@@ -7,10 +7,12 @@ return, and ``dx`` always including ``grad_out`` (the residual branch,
 swiglu_bwd.cu:785-796).  Here the same result comes from five launches of this
 package's sm_100a kernels:
 
-1. ``d_h = grad_out @ W_down`` — the forward linear kernel on the transposed
-   down weight;
-2. ``[d_gate | d_up]`` — ``bell_silu_mul_bwd_bf16`` writes both halves of one
-   ``[T, 2 d_ff]`` buffer;
+1.+2. ``[d_gate | d_up]`` — the forward linear kernel on the transposed down
+   weight computes ``d_h = grad_out @ W_down`` in TMEM and its epilogue
+   applies the SiLU*up backward, writing both halves of one ``[T, 2 d_ff]``
+   buffer (``bell_down_silu_bwd_bf16``; d_h never reaches memory).  With
+   ``fuse_silu=False`` d_h is written in bf16 and ``bell_silu_mul_bwd_bf16``
+   runs as its own pass, the reference's order;
 3. ``dx = [d_gate | d_up] @ [W_gate ; W_up] + grad_out`` — one linear launch
    over the transposed, stacked gate/up weight with ``grad_out`` as the
    residual of its epilogue;
@@ -34,7 +36,7 @@ from typing import Optional, Sequence, Tuple
 import torch
 
 from . import _lib
-from .ops import TILE_IN_OUT, TILE_OUT_IN, _check_cuda, _stream, block_ell_linear
+from .ops import TILE_IN_OUT, TILE_OUT_IN, _check_cuda, _ell, _stream, block_ell_linear, plan_bytes
 
 # (C_blocks, ids of the column-index tensors) -> (weak references, versions, result).
 # A hit needs the very same tensor objects (alive) at the same version: a new
@@ -142,6 +144,32 @@ def silu_mul_bwd(d_h: torch.Tensor, gate_pre: torch.Tensor, up_out: torch.Tensor
     return out
 
 
+def down_silu_bwd(grad_out: torch.Tensor, v_down_t: torch.Tensor, ci_down_t: torch.Tensor, layout_t: int,
+                  gate_pre: torch.Tensor, up_out: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``[d_gate | d_up]`` ([T, 2 d_ff] bf16) from ``grad_out`` and the
+    transposed down weight in one launch (d_h stays in TMEM)."""
+    T, d_model = grad_out.shape
+    R, K, B, _ = v_down_t.shape
+    F = R * B
+    if d_model % B or tuple(gate_pre.shape) != (T, F) or tuple(up_out.shape) != (T, F):
+        raise RuntimeError("grad_out must be [N, C*B] and gate_pre/up_out [N, d_ff]")
+    if out is None:
+        out = torch.empty((T, 2 * F), dtype=torch.bfloat16, device=grad_out.device)
+    if T == 0:
+        return out
+    gate_pre, up_out = gate_pre.contiguous(), up_out.contiguous()
+    plan = torch.empty(plan_bytes(0, 0, 0, R, K), dtype=torch.uint8, device=grad_out.device)
+    d = _lib.BellDownBwdDesc()
+    d.T = T
+    d.grad_out, d.gate_pre, d.up_out = grad_out.data_ptr(), gate_pre.data_ptr(), up_out.data_ptr()
+    d.d_gate_up, d.plan = out.data_ptr(), plan.data_ptr()
+    d.w_t = _ell(v_down_t, ci_down_t, d_model // B, layout_t)
+    d.status = None
+    with torch.cuda.device(grad_out.device):
+        _lib.check(_lib.load().bell_down_silu_bwd_bf16(C.byref(d), _stream()), "down_silu_bwd")
+    return out
+
+
 def block_ell_sddmm(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int, layout: int = TILE_IN_OUT,
                     grad: Optional[torch.Tensor] = None, accumulate: bool = False,
                     out_bf16: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -187,7 +215,7 @@ def block_ell_sddmm(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int
 
 
 def block_ell_swiglu_bwd(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, v_up, ci_up, v_down, ci_down,
-                         layout: int = TILE_IN_OUT, add_residual: bool = True):
+                         layout: int = TILE_IN_OUT, add_residual: bool = True, fuse_silu: bool = True):
     """Returns ``(dx, d_v_gate, d_v_up, d_v_down)`` (bf16) like the reference
     titan::block_ell_swiglu_bwd (block_ell_ops.cpp:83-97).
 
@@ -224,11 +252,13 @@ def block_ell_swiglu_bwd(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, 
     dev = x.device
 
     if T > 0:
-        # 1. d_h = grad_out @ W_down  (transposed down: C_down = R_ff rows)
+        # 1.+2. [d_gate | d_up] from d_h = grad_out @ W_down (transposed down: R_ff rows)
         vdT, cdT, lt = transpose_ell([v_down.contiguous()], [ci_down.contiguous()], R_ff, layout)
-        d_h = block_ell_linear(grad_out, vdT, cdT, layout=lt)
-        # 2. [d_gate | d_up]
-        dgu = silu_mul_bwd(d_h, gate_pre_act, up_out)
+        if fuse_silu:
+            dgu = down_silu_bwd(grad_out, vdT, cdT, lt, gate_pre_act, up_out)
+        else:
+            d_h = block_ell_linear(grad_out, vdT, cdT, layout=lt)
+            dgu = silu_mul_bwd(d_h, gate_pre_act, up_out)
         # 3. dx = [d_gate | d_up] @ [W_gate ; W_up] (+ grad_out)
         vguT, cguT, lt = transpose_ell([v_gate.contiguous(), v_up.contiguous()],
                                        [ci_gate.contiguous(), ci_up.contiguous()], C_model, layout)
