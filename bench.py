@@ -9,6 +9,12 @@ splits the d_ff block-rows across ranks with one NCCL reduce-scatter of the
 down-projection partials (strong scaling: the job size is fixed).
 Rank 0 prints one JSON line.  ``--impl reference`` times the CPU restatement
 of the reference path (oracle/) on the host cores instead.
+
+``--direction bwd`` times the backward of the same FFN instead (one GPU):
+one step = titan::block_ell_swiglu_bwd's work — [d_gate | d_up] (down
+projection fused with the SiLU*up backward), d_x (+ grad_out), and the three
+tile-gradient products — from saved forward intermediates; FLOPs per step are
+twice the forward's.
 """
 
 from __future__ import annotations
@@ -127,6 +133,23 @@ def cpu_baseline_sample(cfg, tokens: int, reps: int = 1):
     return tokens * reps / dt, dt
 
 
+def cpu_backward_sample(cfg, tokens: int):
+    """Time the oracle's tile-by-tile backward (numpy, every host core) on
+    `tokens` tokens of `cfg`; returns tokens/s."""
+    import numpy as np
+    import oracle as O
+    from looped_blockell.synth import make_ffn
+    c = make_ffn(cfg, device="cpu", T=tokens)
+    f = {k: (v.float().numpy() if not k.startswith("c") else v.numpy()) for k, v in c.items()}
+    w = ((f["vg"], f["cg"], 0), (f["vu"], f["cu"], 0), (f["vd"], f["cd"], 0))
+    _, h, g, u = O.swiglu_ffn(f["x"], *w, dtype=np.float32, return_intermediates=True)
+    dy = np.random.default_rng(1).standard_normal(f["x"].shape).astype(np.float32)
+    t0 = time.perf_counter()
+    O.swiglu_ffn_backward_sparse(f["x"], *w, dy, g, u, h, dtype=np.float32)
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt
+
+
 def run_reference(args, cfg, rank, world):
     """CPU arm: the oracle port of the reference path on all host threads."""
     if rank != 0:
@@ -135,24 +158,29 @@ def run_reference(args, cfg, rank, world):
     cores = os.cpu_count()
     sample = args.ref_tokens
     vals = []
-    cpu_baseline_sample(cfg, sample // 4)  # warm-up (untimed)
-    for _ in range(max(args.warmup, 0)):
-        pass
+    bwd = args.direction == "bwd"
+    fn = cpu_backward_sample if bwd else cpu_baseline_sample
+    if bwd:
+        sample = max(64, sample // 4)  # the backward does twice the work per token
+    fn(cfg, max(8, sample // 4))  # warm-up (untimed)
     for _ in range(args.steps):
-        v, _ = cpu_baseline_sample(cfg, sample)
+        v, _ = fn(cfg, sample)
         vals.append(v)
     value = statistics.median(vals)
     ms = cfg.T / value * 1e3
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC + (" (backward)" if bwd else ""), "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": cfg.name, "T": cfg.T, "d_model": cfg.d_model, "d_ff": cfg.d_ff, "B": cfg.B,
-                   "density": cfg.density, "sample_tokens": sample},
-        "tflops_effective": cfg.nnz_flops() / (ms / 1e3) / 1e12,
+                   "density": cfg.density, "sample_tokens": sample, "direction": args.direction},
+        "tflops_effective": (2 if bwd else 1) * cfg.nnz_flops() / (ms / 1e3) / 1e12,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} tokens of {cfg.name} per step, numpy gather+BLAS restatement of "
-                                   f"block_ell_matmul (oracle/bell_oracle.py), scaled linearly to T={cfg.T}"},
+                         "sample": f"{sample} tokens of {cfg.name} per step, numpy "
+                                   + ("tile-by-tile restatement of the reference backward "
+                                      "(swiglu_ffn_backward_sparse)" if bwd else
+                                      "gather+BLAS restatement of block_ell_matmul")
+                                   + f" (oracle/bell_oracle.py), scaled linearly to T={cfg.T}"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -172,6 +200,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
+    ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd"], help="time the forward or the backward")
     args = ap.parse_args()
     from looped_blockell.synth import CONFIGS
     cfg = CONFIGS[args.config]
@@ -183,7 +212,126 @@ def main():
     if args.impl == "reference":
         run_reference(args, cfg, rank, world)
         return
+    if args.direction == "bwd":
+        if cfg.dtype != "bf16" or cfg.L != 1:
+            raise SystemExit("--direction bwd: the backward exists for the bf16 SwiGLU configs (2, 5)")
+        run_gpu_bwd(args, cfg, rank, world)
+        return
     run_gpu(args, cfg, rank, world)
+
+
+def run_gpu_bwd(args, cfg, rank, world):
+    """One backward step per iteration on one GPU (replicas under torchrun:
+    each rank times its own copy, max over ranks)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from looped_blockell.kernels import backward as kb
+    from looped_blockell.kernels import ops
+    from looped_blockell.synth import make_ffn
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
+    c = make_ffn(cfg, device="cuda", shared_gate_up=args.shared_gate_up)
+    lay = ops.TILE_OUT_IN if args.layout == "out_in" else ops.TILE_IN_OUT
+    if lay == ops.TILE_OUT_IN:
+        for k in ("vg", "vu", "vd"):
+            c[k] = c[k].transpose(-1, -2).contiguous()
+    T, d, F, B = cfg.T, cfg.d_model, cfg.d_ff, cfg.B
+    x = c["x"]
+    _, h, g, u = ops.block_ell_swiglu_fwd_with_intermediate(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"],
+                                                            add_residual=True, layout=lay)
+    dy = torch.randn(T, d, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda").to(torch.bfloat16)
+    w = (c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"])
+
+    def step():
+        return kb.block_ell_swiglu_bwd(dy, x, g, u, h, *w, layout=lay)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        gpu_id = str(local)
+    evs = [_events(torch) for _ in range(args.steps)]
+    with ClockSampler(gpu_id) as clk:
+        for a, b in evs:
+            a.record()
+            step()
+            b.record()
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2.0 * cfg.nnz_flops()
+    tflops = flops / (ms / 1e3) / 1e12
+
+    # the kernels of one step, each timed alone with events
+    vdT, cdT, lt = kb.transpose_ell([c["vd"]], [c["cd"]], F // B, lay)
+    vguT, cguT, lt2 = kb.transpose_ell([c["vg"], c["vu"]], [c["cg"], c["cu"]], d // B, lay)
+    dgu = kb.down_silu_bwd(dy, vdT, cdT, lt, g, u)
+    dh = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
+    g32 = torch.empty(c["vg"].shape, dtype=torch.float32, device="cuda")
+    d32 = torch.empty(c["vd"].shape, dtype=torch.float32, device="cuda")
+    parts = {
+        "transpose_gather": lambda: (kb.transpose_ell([c["vd"]], [c["cd"]], F // B, lay),
+                                     kb.transpose_ell([c["vg"], c["vu"]], [c["cg"], c["cu"]], d // B, lay)),
+        "down_silu_bwd": lambda: kb.down_silu_bwd(dy, vdT, cdT, lt, g, u, out=dgu),
+        "unfused_d_h_linear": lambda: ops.block_ell_linear(dy, vdT, cdT, layout=lt, out=dh),
+        "unfused_silu_mul_bwd": lambda: kb.silu_mul_bwd(dh, g, u, out=dgu),
+        "dx_linear": lambda: ops.block_ell_linear(dgu, vguT, cguT, residual=dy, layout=lt2),
+        "sddmm_gate": lambda: kb.block_ell_sddmm(x, dgu[:, :F], c["cg"], B, lay, grad=g32),
+        "sddmm_down": lambda: kb.block_ell_sddmm(h, dy, c["cd"], B, lay, grad=d32),
+    }
+    part_ms = {}
+    for name, fn in parts.items():
+        fn()
+        a, b = _events(torch)
+        a.record()
+        for _ in range(5):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        part_ms[name] = a.elapsed_time(b) / 5
+    R_f, R_d = F // B, d // B
+    sd_flops = 2.0 * T * B * B * R_f * cfg.K_gu  # one gate (or up) tile-gradient launch
+    sd_tf = sd_flops / (part_ms["sddmm_gate"] / 1e3) / 1e12
+
+    if rank == 0:
+        line = {
+            "metric": METRIC + " (backward)", "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "direction": "bwd", "T": T, "d_model": d, "d_ff": F, "B": B,
+                       "density": cfg.density, "tile_layout": args.layout,
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (x, g, u, h, grad_out resident)"},
+            "tflops_effective": tflops, "flops_per_step": flops,
+            "kernels_ms": part_ms,
+            "roofline": {"bound": "tensor", "kernel": "whole backward step", "achieved": tflops, "peak": tc_peak,
+                         "unit": "TFLOP/s", "frac": tflops / tc_peak, "peak_source": f"{peak_src} bf16 burst",
+                         "traffic": None, "sddmm_gate_tflops": sd_tf, "sddmm_gate_frac": sd_tf / tc_peak},
+            "gpu_launches": 10 * args.steps,
+            "clocks": clk.summary(), "e2e": None,
+        }
+        if world == 1 and not args.no_cpu:
+            v, dt = cpu_backward_sample(cfg, max(64, args.cpu_tokens // 4))
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"{max(64, args.cpu_tokens // 4)} tokens of {cfg.name} ({dt:.1f} s), "
+                                              "numpy tile-by-tile restatement of the reference backward"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def _events(torch):

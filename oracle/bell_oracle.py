@@ -28,7 +28,8 @@ LAYOUT_OUT_IN = 1
 __all__ = [
     "LAYOUT_IN_OUT", "LAYOUT_OUT_IN",
     "random_topology", "block_ell_to_dense", "dense_to_block_ell",
-    "block_ell_matmul", "silu", "swiglu_ffn", "swiglu_ffn_backward", "rmsnorm", "looped_ffn",
+    "block_ell_matmul", "block_ell_matmul_t", "silu", "swiglu_ffn", "swiglu_ffn_backward",
+    "swiglu_ffn_backward_sparse", "rmsnorm", "looped_ffn",
     "ternary_quantize_tiles", "activation_quantize_int", "pack_ternary",
     "unpack_ternary", "ternary_block_ell_matmul", "ternary_swiglu_ffn",
     "bf16_round", "rel_l2", "nnz_flops",
@@ -156,6 +157,25 @@ def block_ell_matmul(x: np.ndarray, values: np.ndarray, cols: np.ndarray,
     return y
 
 
+def block_ell_matmul_t(y: np.ndarray, values: np.ndarray, cols: np.ndarray, in_features: int,
+                       layout: int = LAYOUT_IN_OUT, dtype=np.float64) -> np.ndarray:
+    """``dx = dy @ W`` for the Block-ELL W of ``block_ell_matmul`` (the input
+    gradient of y = x W^T): ``dx[:, c(r,k) block] += dy[:, r block] @ V[r,k]^T``
+    for [B_in, B_out] tiles.  The reference computes it by scattering per slot
+    (csrc/block_ell/swiglu_bwd.cu:7-12, 16-24); restated with one GEMM per slot."""
+    tiles = _tile_in_out(values, layout)
+    R, K, B, _ = tiles.shape
+    y = np.asarray(y, dtype=dtype)
+    dx = np.zeros((y.shape[0], in_features), dtype=dtype)
+    for r in range(R):
+        yr = y[:, r * B:(r + 1) * B]
+        for k in range(K):
+            c = int(cols[r, k])
+            if c >= 0:
+                dx[:, c * B:(c + 1) * B] += yr @ tiles[r, k].astype(dtype).T
+    return dx
+
+
 def silu(a: np.ndarray) -> np.ndarray:
     """x * sigmoid(x) (jax.nn.silu / F.silu)."""
     return a / (1.0 + np.exp(-a))
@@ -231,6 +251,41 @@ def swiglu_ffn_backward(x, gate, up, down, dy, add_residual=True):
         dx = dx + dyv
     return (dx, _tile_grads(dg.T @ xv, cg, B, lg), _tile_grads(du.T @ xv, cu, B, lu),
             _tile_grads(dyv.T @ h, cd, B, ld))
+
+
+def swiglu_ffn_backward_sparse(x, gate, up, down, dy, g, u, h, add_residual=True, dtype=np.float64):
+    """The same gradients as ``swiglu_ffn_backward`` from the saved forward
+    intermediates (g = gate pre-activation, u = up output, h = silu(g) * u),
+    as the reference op takes them (block_ell_ops.cpp:83-97), computed tile by
+    tile: transposed Block-ELL products for d_h and d_x and one
+    a[:, c]^T b[:, r] product per live slot for the tile gradients
+    (swiglu_bwd.cu:13-14, 29-30).  Cost grows with the live tiles, not with
+    d_model * d_ff, so it serves as the CPU timing arm too."""
+    x, dy, g, u, h = (np.asarray(a, dtype=dtype) for a in (x, dy, g, u, h))
+    (vg, cg, lg), (vu, cu, lu), (vd, cd, ld) = gate, up, down
+    d = x.shape[1]
+    F = g.shape[1]
+    dh = block_ell_matmul_t(dy, vd, cd, F, ld, dtype)
+    sig = 1.0 / (1.0 + np.exp(-g))
+    dg = dh * u * (sig + g * sig * (1.0 - sig))
+    du = dh * g * sig
+    dx = block_ell_matmul_t(dg, vg, cg, d, lg, dtype) + block_ell_matmul_t(du, vu, cu, d, lu, dtype)
+    if add_residual:
+        dx = dx + dy
+
+    def tile_grads(a, b, values, cols, layout):
+        R, K, B, _ = values.shape
+        out = np.zeros((R, K, B, B), dtype=dtype)
+        for r in range(R):
+            br = b[:, r * B:(r + 1) * B]
+            for k in range(K):
+                c = int(cols[r, k])
+                if c >= 0:
+                    t = a[:, c * B:(c + 1) * B].T @ br  # [B_in, B_out]
+                    out[r, k] = t if layout == LAYOUT_IN_OUT else t.T
+        return out
+
+    return (dx, tile_grads(x, dg, vg, cg, lg), tile_grads(x, du, vu, cu, lu), tile_grads(h, dy, vd, cd, ld))
 
 
 def rmsnorm(x: np.ndarray, gain: np.ndarray, eps: float = 1e-5, dtype=np.float64) -> np.ndarray:
