@@ -11,8 +11,9 @@ Rank 0 prints one JSON line.  ``--impl reference`` times the CPU restatement
 of the reference path (oracle/) on the host cores instead.
 
 ``--direction bwd`` times the backward of the same FFN instead (one GPU):
-one step = titan::block_ell_swiglu_bwd's work — [d_gate | d_up] (down
-projection fused with the SiLU*up backward), d_x (+ grad_out), and the three
+one step = titan::block_ell_swiglu_bwd's work — [d_gate | d_up] (at tile
+size 64 the down projection fused with the SiLU*up backward, at 128 the two
+as separate launches), d_x (+ grad_out), and the three
 tile-gradient products — from saved forward intermediates; FLOPs per step are
 twice the forward's.
 """
@@ -320,7 +321,7 @@ def run_gpu_bwd(args, cfg, rank, world):
             "roofline": {"bound": "tensor", "kernel": "whole backward step", "achieved": tflops, "peak": tc_peak,
                          "unit": "TFLOP/s", "frac": tflops / tc_peak, "peak_source": f"{peak_src} bf16 burst",
                          "traffic": None, "sddmm_gate_tflops": sd_tf, "sddmm_gate_frac": sd_tf / tc_peak},
-            "gpu_launches": 10 * args.steps,
+            "gpu_launches": (10 if B == 64 else 11) * args.steps,
             "clocks": clk.summary(), "e2e": None,
         }
         if world == 1 and not args.no_cpu:

@@ -10,12 +10,13 @@
 //     d_up = d_h * silu(gate) (swiglu_bwd.cu:305-334);
 //   * bell_sddmm_kernel: the tile gradients d_W[r, k] = a[:, c]^T b[:, r]
 //     summed over tokens (swiglu_bwd.cu:13-14, 29-30), on tcgen05 with the
-//     token dimension as the MMA K: A = a's 128 feature columns of the tile
-//     (two 64-wide groups), B = b's B feature columns, both MN-major straight
-//     from the row-major activations.  Token ranges are split across CTAs
-//     and the fp32 partial tiles are added into the gradient with vector
-//     atomics.  At tile size 64 a work unit covers two slots of one row (the
-//     two 64-feature groups of A come from two column blocks), so M is 128.
+//     token dimension as the MMA K and both operands MN-major straight from
+//     the row-major activations.  A work unit is two slots of one block-row:
+//     at tile size 64 the two slots' a features form M = 128 against the
+//     row's 64 b features; at 128 the row's b features are M and the two
+//     slots' a features N = 256, so one b chunk serves both slots.  Tokens
+//     run in ranges sized to stay in L2; each CTA takes an equal share of a
+//     range and adds its fp32 partial tiles into the gradient with atomics.
 #include <string>
 
 #include "bell_bf16.cuh"
@@ -64,17 +65,26 @@ __global__ void __launch_bounds__(256) bell_f32_to_bf16_kernel(const float* __re
 
 // ------------------------------------------------------------------ SDDMM
 
-static constexpr int kTok = 64;                // tokens per stage (MMA K per stage)
-static constexpr int kABytes = kTok * 128 * 2;  // 16 KB: 64 tokens x 128 features of a
+static constexpr int kTok = 64;   // tokens per stage (MMA K per stage)
 static constexpr int kThr = 192;  // warp 0 producer, 1 MMA, 2-5 epilogue
 
+// A unit is two slots of one block-row.  B = 64: M = the two slots' a
+// features (2 x 64), N = the row's 64 b features.  B = 128 (TR): M = the
+// row's 128 b features, N = the two slots' a features (2 x 128), so the b
+// chunk is loaded once for both slots.  Both operands are MN-major straight
+// from the row-major activations: 64-token x 64-feature boxes, 128-byte
+// swizzle, 64-feature groups 8 KB apart.
 template <int B>
 struct SCfg {
-  static constexpr int B_BYTES = kTok * B * 2;  // 8 / 16 KB: 64 tokens x B features of b
-  static constexpr int STAGE = kABytes + B_BYTES;
-  static constexpr int NS = 196608 / STAGE;     // 8 / 6 stages
+  static constexpr bool TR = B == 128;
+  static constexpr int SLOTS = 2;
+  static constexpr int A_BYTES = 16384;                // B=64: two a slots; B=128: b
+  static constexpr int B_BYTES = TR ? 32768 : 8192;    // B=64: b; B=128: two a slots
+  static constexpr int STAGE = A_BYTES + B_BYTES;      // 24 / 48 KB
+  static constexpr int N = TR ? 256 : 64;              // MMA N = accumulator columns
+  static constexpr int NS = 196608 / STAGE;            // 8 / 4 stages
   static constexpr int SMEM = NS * STAGE + 1024 + 512;
-  static constexpr int SLOTS = B == 64 ? 2 : 1;  // slots of one row per unit
+  static constexpr int TMEM_COLS = 2 * N;              // two accumulators
 };
 
 struct SddmmParams {
@@ -197,7 +207,7 @@ __global__ void __launch_bounds__(kThr, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * B);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -236,22 +246,23 @@ __global__ void __launch_bounds__(kThr, 1)
           }
           uint8_t* st = smem + stage * C::STAGE;
           const int y = int(ch * kTok);
-          uint32_t bytes = C::B_BYTES;
-          if (B == 128) bytes += x.c0 >= 0 ? kABytes : 0;
-          else bytes += (x.c0 >= 0 ? kABytes / 2 : 0) + (x.c1 >= 0 ? kABytes / 2 : 0);
+          constexpr uint32_t SLOT_BYTES = C::TR ? 16384 : 8192;  // one slot's a chunk
+          const uint32_t bytes = (C::TR ? 16384 : 8192) + (x.c0 >= 0 ? SLOT_BYTES : 0) + (x.c1 >= 0 ? SLOT_BYTES : 0);
           mbar_arrive_expect_tx(&full[stage], bytes);
-          if (B == 128) {
-            if (x.c0 >= 0) {
-              tma_load_2d(st, &tm_a, &full[stage], x.c0 * 128, y, pol);
-              tma_load_2d(st + 8192, &tm_a, &full[stage], x.c0 * 128 + 64, y, pol);
-            }
-          } else {
-            if (x.c0 >= 0) tma_load_2d(st, &tm_a, &full[stage], x.c0 * 64, y, pol);
-            if (x.c1 >= 0) tma_load_2d(st + 8192, &tm_a, &full[stage], x.c1 * 64, y, pol);
+          // a slots: B=64 -> A operand groups 0 / 1; B=128 -> B operand, 16 KB each
+          uint8_t* a_dst = st + (C::TR ? C::A_BYTES : 0);
+          uint8_t* b_dst = st + (C::TR ? 0 : C::A_BYTES);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int c = j == 0 ? x.c0 : x.c1;
+            if (c < 0) continue;
+#pragma unroll
+            for (int h = 0; h < B / 64; ++h)
+              tma_load_2d(a_dst + j * SLOT_BYTES + h * 8192, &tm_a, &full[stage], c * B + h * 64, y, pol);
           }
 #pragma unroll
           for (int h = 0; h < B / 64; ++h)
-            tma_load_2d(st + kABytes + h * 8192, &tm_b, &full[stage], x.r * B + h * 64, y, pol);
+            tma_load_2d(b_dst + h * 8192, &tm_b, &full[stage], x.r * B + h * 64, y, pol);
           last = stage;
           last_phase = phase;
           if (++stage == C::NS) {
@@ -278,9 +289,9 @@ __global__ void __launch_bounds__(kThr, 1)
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer
     const bool leader = elect_one();
-    constexpr uint32_t IDESC = idesc_bf16(128, B, true, true);
+    constexpr uint32_t IDESC = idesc_bf16(128, C::N, true, true);
     const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem), 8192, 1024);
-    const uint64_t b_desc0 = sdesc_sw128(smem_u32(smem) + kABytes, 8192, 1024);
+    const uint64_t b_desc0 = sdesc_sw128(smem_u32(smem) + C::A_BYTES, 8192, 1024);
     int stage = 0, i = 0;
     uint32_t phase = 0;
     SegIt it = seg_begin(p);
@@ -294,7 +305,7 @@ __global__ void __launch_bounds__(kThr, 1)
       ++i;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl))) break;
       tc_fence_after();
-      const uint32_t d = tmem + uint32_t(buf * B);
+      const uint32_t d = tmem + uint32_t(buf * C::N);
       bool ok = true;
       for (int64_t ch = a0; ch < a1; ++ch) {
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ctl))) {
@@ -332,7 +343,7 @@ __global__ void __launch_bounds__(kThr, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int row = q * 32 + lane;  // accumulator row = feature of a
+    const int row = q * 32 + lane;  // accumulator row (TMEM lane)
     int i = 0;
     SegIt it = seg_begin(p);
     Unit x;
@@ -345,26 +356,54 @@ __global__ void __launch_bounds__(kThr, 1)
       ++i;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1u, ctl))) break;
       tc_fence_after();
-      // the rows of this warp belong to one slot: at B=64 rows 64-127 are the second slot
-      const int k = (B == 64 && q >= 2) ? x.k1 : x.k0;
-      const int c = (B == 64 && q >= 2) ? x.c1 : x.c0;
-      const int trow = B == 64 ? (row & 63) : row;
-      float* tile = p.grad + (size_t(x.r) * p.K + (k >= 0 ? k : 0)) * B * B;
-      const uint32_t tb = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * B);
+      const uint32_t tb = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * C::N);
+      if constexpr (!C::TR) {
+        // B = 64: accumulator row = a feature; rows 0-63 slot k0, 64-127 slot k1;
+        // columns = the row's 64 b (output) features
+        const int k = q >= 2 ? x.k1 : x.k0;
+        const int c = q >= 2 ? x.c1 : x.c0;
+        const int fin = row & 63;
+        float* tile = p.grad + (size_t(x.r) * p.K + (k >= 0 ? k : 0)) * B * B;
 #pragma unroll 1
-      for (int j = 0; j < B / 32; ++j) {
-        uint32_t v[32];
-        tmem_ld32_sync(tb + j * 32, v);
-        if (c < 0) continue;
-        if (!p.out_in) {  // [B_in, B_out]: this row's 32 outputs are contiguous
-          float* dst = tile + size_t(trow) * B + j * 32;
+        for (int j = 0; j < B / 32; ++j) {
+          uint32_t v[32];
+          tmem_ld32_sync(tb + j * 32, v);
+          if (c < 0) continue;
+          if (!p.out_in) {  // [B_in, B_out]: this row's 32 outputs are contiguous
+            float* dst = tile + size_t(fin) * B + j * 32;
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            red_add_v4(dst + 4 * t, __uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
-                       __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
-        } else {  // [B_out, B_in]: consecutive lanes hit consecutive addresses
+            for (int t = 0; t < 8; ++t)
+              red_add_v4(dst + 4 * t, __uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                         __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
+          } else {  // [B_out, B_in]: consecutive lanes hit consecutive addresses
 #pragma unroll
-          for (int t = 0; t < 32; ++t) atomicAdd(tile + size_t(j * 32 + t) * B + trow, __uint_as_float(v[t]));
+            for (int t = 0; t < 32; ++t) atomicAdd(tile + size_t(j * 32 + t) * B + fin, __uint_as_float(v[t]));
+          }
+        }
+      } else {
+        // B = 128: accumulator row = b (output) feature `row`; columns 0-127
+        // slot k0's a (input) features, 128-255 slot k1's
+#pragma unroll 1
+        for (int sl = 0; sl < 2; ++sl) {
+          const int k = sl ? x.k1 : x.k0;
+          const int c = sl ? x.c1 : x.c0;
+          if (c < 0) continue;  // warp-uniform
+          float* tile = p.grad + (size_t(x.r) * p.K + k) * B * B;
+#pragma unroll 1
+          for (int j = 0; j < B / 32; ++j) {
+            uint32_t v[32];
+            tmem_ld32_sync(tb + sl * B + j * 32, v);
+            if (!p.out_in) {  // [B_in, B_out]: consecutive lanes hit consecutive addresses
+#pragma unroll
+              for (int t = 0; t < 32; ++t) atomicAdd(tile + size_t(j * 32 + t) * B + row, __uint_as_float(v[t]));
+            } else {  // [B_out, B_in]: this row's 32 inputs are contiguous
+              float* dst = tile + size_t(row) * B + j * 32;
+#pragma unroll
+              for (int t = 0; t < 8; ++t)
+                red_add_v4(dst + 4 * t, __uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                           __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
+            }
+          }
         }
       }
       tc_fence_before();
@@ -377,7 +416,7 @@ __global__ void __launch_bounds__(kThr, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * B);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
@@ -409,10 +448,13 @@ int launch_sddmm(const BellSddmmDesc* d, int32_t* status, cudaStream_t s, int sm
   p.C = d->C;
   const int64_t chunks = (d->T + kTok - 1) / kTok;
   const int64_t per = int64_t(p.R) * p.KP;
-  // token ranges of 4096 tokens: the activations of one range stay in L2
-  // while every unit passes over them; each CTA's share of a range adds a
-  // few partial tiles, small next to its loads
-  const int64_t range = 64;
+  // token ranges whose operands (a and b rows, bf16) fit in ~96 MB of the
+  // 126 MB L2, so every unit of the range re-reads them from L2; 16..128
+  // chunks (1024..8192 tokens) keep each CTA's partial-tile additions small
+  // next to its loads
+  const int64_t row_bytes = 2 * (int64_t(d->C) + d->R) * B;
+  int64_t range = (int64_t(96) << 20) / (row_bytes * kTok);
+  range = range < 16 ? 16 : (range > 128 ? 128 : range);
   p.split_chunks = chunks < range ? chunks : range;
   p.n_split = int32_t((chunks + p.split_chunks - 1) / p.split_chunks);
   p.cols = d->col_indices;
