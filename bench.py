@@ -201,7 +201,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
-    ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd"], help="time the forward or the backward")
+    ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd", "convert"],
+                    help="time the forward, the backward, or the dense -> Block-ELL conversion of the gate weight")
     args = ap.parse_args()
     from looped_blockell.synth import CONFIGS
     cfg = CONFIGS[args.config]
@@ -212,6 +213,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         run_reference(args, cfg, rank, world)
+        return
+    if args.direction == "convert":
+        run_convert(args, cfg, rank, world)
         return
     if args.direction == "bwd":
         if cfg.dtype != "bf16" or cfg.L != 1:
@@ -333,6 +337,64 @@ def run_gpu_bwd(args, cfg, rank, world):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_convert(args, cfg, rank, world):
+    """Dense -> Block-ELL conversion of one gate-shaped weight [d_ff, d_model]
+    (bf16) per step, on one GPU; HBM-bound: the matrix is read once and the
+    kept tiles written once."""
+    import numpy as np
+    import torch
+    from looped_blockell.kernels import convert as kc
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(0)
+    hbm_peak, _, _, peak_src = load_peaks()
+    d, F, B = cfg.d_model, cfg.d_ff, cfg.B
+    g = torch.Generator(device="cuda").manual_seed(0)
+    dense = (torch.randn(F, d, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    K = max(1, int((d // B) * cfg.density))
+    for _ in range(args.warmup):
+        kc.dense_to_block_ell(dense, B, K=K)
+    torch.cuda.synchronize()
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(0).uuid)
+    except Exception:
+        gpu_id = "0"
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    evs = [_events(torch) for _ in range(args.steps)]
+    with ClockSampler(gpu_id) as clk:
+        for a, b in evs:
+            flush.fill_(1)
+            a.record()
+            kc.dense_to_block_ell(dense, B, K=K)
+            b.record()
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    R, C = F // B, d // B
+    alg = 2.0 * F * d + 2.0 * R * K * B * B + 4.0 * R * C * 2 + 4.0 * R * K  # dense, values, norms w+r, cols
+    gbs = alg / (ms / 1e3) / 1e9
+    line = {"metric": "dense -> Block-ELL conversion (create_block_ell_from_dense)", "value": 2.0 * F * d / (ms / 1e3) / 1e9,
+            "unit": "GB/s of dense input", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{cfg.name} gate weight", "out_features": F, "in_features": d, "B": B, "K": K,
+                       "l2": "L2 flushed between steps (256 MiB write outside the timed events)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "peak_source": f"{peak_src} copy bandwidth", "traffic": None,
+                         "note": "algorithmic bytes: dense read + kept tiles written + norms + cols"},
+            "gpu_launches": 3 * args.steps, "clocks": clk.summary(), "e2e": None}
+    if not args.no_cpu:
+        import oracle as O
+        dn = dense[: min(F, 2048)].float().cpu().numpy()
+        t0 = time.perf_counter()
+        O.dense_to_block_ell(dn, B, K / C)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": dn.nbytes / 2 / dt / 1e9, "unit": "GB/s of dense input (bf16 bytes)",
+                                "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{dn.shape[0]} x {dn.shape[1]} rows of the same matrix ({dt:.2f} s), numpy "
+                                          "restatement (oracle dense_to_block_ell)"}
+    print(json.dumps(line), flush=True)
 
 
 def _events(torch):

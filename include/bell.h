@@ -317,6 +317,29 @@ typedef struct BellSddmmDesc {
 
 int bell_sddmm_bf16(const BellSddmmDesc* desc, void* stream);
 
+/* ------------------------------------------------------------- conversion */
+
+/*
+ * Dense weight [out_features, in_features] -> Block-ELL keeping, per block-row,
+ * the K tiles of largest Frobenius norm (ties: the lower column first), kept
+ * columns ascending.  Replaces create_block_ell_from_dense
+ * (looped_blockell/layers/block_ell.py:79-116; K = max(1, int(C * density))
+ * is the caller's).  dense: bf16 or f32 row-major, 16-byte aligned; values:
+ * [R, K, B, B] same type, in `layout`; col_indices: [R, K]; norms: [R, C]
+ * f32 workspace that receives the tile norms.  B is 64 or 128, C <= 2048.
+ */
+typedef struct BellDenseToEllDesc {
+  const void* dense;
+  int32_t dtype;               /* BELL_DTYPE_BF16 / BELL_DTYPE_F32 */
+  int32_t out_features, in_features;
+  int32_t B, K, layout;
+  void* values;
+  int32_t* col_indices;
+  float* norms;
+} BellDenseToEllDesc;
+
+int bell_dense_to_ell(const BellDenseToEllDesc* desc, void* stream);
+
 /* ---------------------------------------------------------------- L2 pins */
 
 /* Persisting-L2 window over [base, base+bytes) on `stream`; replaces

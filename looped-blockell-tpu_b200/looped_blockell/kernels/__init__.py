@@ -13,6 +13,7 @@ from .loop import (diagonal_injection, looped_ffn, persistent_mlp_step, pin_weig
                    unpin_weights_l2)
 from .backward import (block_ell_sddmm, block_ell_swiglu, block_ell_swiglu_bwd, down_silu_bwd,  # noqa: F401
                        silu_mul_bwd, transpose_ell, transposed_topology)
+from .convert import dense_to_block_ell  # noqa: F401
 from .stream import block_ell_swiglu_fwd_host, looped_ffn_host, pipeline_tokens  # noqa: F401
 from . import torch_ops as _torch_ops
 

@@ -77,6 +77,12 @@ class BellSddmmDesc(C.Structure):
                 ("grad_bf16", C.c_void_p), ("status", C.c_void_p)]
 
 
+class BellDenseToEllDesc(C.Structure):
+    _fields_ = [("dense", C.c_void_p), ("dtype", C.c_int32), ("out_features", C.c_int32),
+                ("in_features", C.c_int32), ("B", C.c_int32), ("K", C.c_int32), ("layout", C.c_int32),
+                ("values", C.c_void_p), ("col_indices", C.c_void_p), ("norms", C.c_void_p)]
+
+
 # every exported symbol of include/bell.h: name -> (restype, argtypes)
 SIGNATURES = {
     "bell_abi_version": (C.c_int, []),
@@ -103,6 +109,7 @@ SIGNATURES = {
                                          C.c_void_p, C.c_int64, C.c_void_p]),
     "bell_down_silu_bwd_bf16": (C.c_int, [C.POINTER(BellDownBwdDesc), C.c_void_p]),
     "bell_sddmm_bf16": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
+    "bell_dense_to_ell": (C.c_int, [C.POINTER(BellDenseToEllDesc), C.c_void_p]),
     "bell_pin_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "bell_unpin_l2": (C.c_int, [C.c_void_p]),
 }

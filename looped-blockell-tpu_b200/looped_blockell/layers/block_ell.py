@@ -85,13 +85,23 @@ def create_random_topology(R: int, C: int, K: int, key: Union[int, torch.Generat
 
 def create_block_ell_from_dense(dense: torch.Tensor, tile_size: int = 16, density: float = 0.5) -> BlockELLTensor:
     """Dense ``[out, in]`` -> Block-ELL keeping the top-K Frobenius-norm tiles
-    per block-row, columns sorted (reference block_ell.py:79-116)."""
+    per block-row, columns sorted (reference block_ell.py:79-116).
+
+    A CUDA bf16/fp32 matrix with the kernels' tile sizes (64, 128) is
+    converted by ``kernels.convert.dense_to_block_ell`` (two sm_100a
+    launches).  Other tile sizes and host tensors — the reference's JAX code
+    runs this step wherever the weights live — use the tensor expression
+    below, which computes the same thing."""
     out_f, in_f = dense.shape
     B = tile_size
     if out_f % B != 0 or in_f % B != 0:
         raise ValueError(f"Dimensions ({out_f}, {in_f}) must be divisible by tile_size {B}")
     R, C = out_f // B, in_f // B
     K = max(1, int(C * density))
+    if dense.is_cuda and B in (64, 128) and dense.dtype in (torch.bfloat16, torch.float32) and C <= 2048:
+        from ..kernels.convert import dense_to_block_ell
+        values, cols, _ = dense_to_block_ell(dense, B, K=K)
+        return BlockELLTensor(values=values, col_indices=cols, config=BlockELLConfig(R=R, C=C, K=K, B=B))
     blocks = dense.reshape(R, B, C, B).permute(0, 2, 3, 1)  # [R, C, B_in, B_out]
     norms = blocks.float().pow(2).sum(dim=(2, 3)).sqrt()
     top = torch.argsort(-norms, dim=1, stable=True)[:, :K]

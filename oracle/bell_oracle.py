@@ -28,7 +28,7 @@ LAYOUT_OUT_IN = 1
 __all__ = [
     "LAYOUT_IN_OUT", "LAYOUT_OUT_IN",
     "random_topology", "block_ell_to_dense", "dense_to_block_ell",
-    "block_ell_matmul", "block_ell_matmul_t", "silu", "swiglu_ffn", "swiglu_ffn_backward",
+    "compact_block_ell", "dff_permutation", "block_ell_matmul", "block_ell_matmul_t", "silu", "swiglu_ffn", "swiglu_ffn_backward",
     "swiglu_ffn_backward_sparse", "rmsnorm", "looped_ffn",
     "ternary_quantize_tiles", "activation_quantize_int", "pack_ternary",
     "unpack_ternary", "ternary_block_ell_matmul", "ternary_swiglu_ffn",
@@ -127,6 +127,32 @@ def dense_to_block_ell(dense: np.ndarray, tile_size: int, density: float):
     cols = np.sort(top, axis=1).astype(np.int32)
     values = np.stack([blocks[r, cols[r]] for r in range(R)])
     return values, cols
+
+
+def compact_block_ell(values: np.ndarray, cols: np.ndarray, alive: np.ndarray):
+    """Pack alive slots to the front of each row (stable), cut to
+    K_new = max(1, max alive count).  Follows looped_blockell/opt/compaction.py:
+    31-61 (argsort of ~alive, truncate; dead survivors keep index and tile).
+    Returns (values, cols, alive, K_new)."""
+    alive = np.asarray(alive, dtype=bool)
+    K_new = max(1, int(alive.sum(axis=1).max()) if alive.shape[0] else 1)
+    order = np.argsort(~alive, axis=1, kind="stable")[:, :K_new]
+    rows = np.arange(cols.shape[0])[:, None]
+    return values[rows, order], cols[rows, order], alive[rows, order], K_new
+
+
+def dff_permutation(fc1_alive, fc2_alive, fc1_cols, C_ff: int) -> np.ndarray:
+    """d_ff order by descending importance: alive fc1 tiles per column plus
+    alive fc2 tiles per block-row (looped_blockell/opt/column_reorder.py:36-120).
+    Returns perm with perm[new] = old."""
+    imp = np.zeros(C_ff, dtype=np.float64)
+    for c, a in zip(np.asarray(fc1_cols).reshape(-1), np.asarray(fc1_alive).reshape(-1)):
+        if c >= 0 and a:
+            imp[min(int(c), C_ff - 1)] += 1.0
+    rows = np.asarray(fc2_alive, dtype=np.float64).sum(axis=1)
+    n = min(rows.shape[0], C_ff)
+    imp[:n] += rows[:n]
+    return np.argsort(-imp, kind="stable").astype(np.int32)
 
 
 # ----------------------------------------------------------------------------
