@@ -240,6 +240,15 @@ int bell_loop_fwd_bf16(const BellLoopDesc* desc, void* stream);
 int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const void* e,
                              const float* log_A, const float* log_dt, void* out, void* stream);
 
+/* Injection fused with the first RMSNorm of persistent_mlp_step:
+ * h_out = injection(h, e) (bf16, the residual base) and
+ * normed = RMSNorm(h_out) * gain, in one pass; bit-identical to
+ * bell_diag_injection_bf16 followed by bell_rmsnorm_bf16.  d_model % 8 == 0,
+ * bf16 pointers 16-byte aligned. */
+int bell_inject_rmsnorm_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,
+                             const float* log_dt, const void* gain, float eps, void* h_out, void* normed,
+                             void* stream);
+
 /* RMSNorm (bf16 in/out, fp32 math); replaces rmsnorm_cuda
  * (csrc/loop/persistent_core.cu:97-154,224-264). */
 int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gain, float eps,

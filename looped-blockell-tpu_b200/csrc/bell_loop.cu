@@ -69,6 +69,65 @@ __global__ void __launch_bounds__(256) bell_injection_kernel(const __nv_bfloat16
   }
 }
 
+// Injection and the first RMSNorm of persistent_mlp_step in one pass: one
+// warp per token row writes the injected h (bf16, the residual base) and
+// normalises those bf16 values, so the result is bit-identical to the two
+// kernels above run back to back.  Each lane reads back only what it wrote.
+__global__ void __launch_bounds__(256) bell_inject_rmsnorm_kernel(
+    const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ e, const float* __restrict__ log_A,
+    const float* __restrict__ log_dt, const __nv_bfloat16* __restrict__ gain, __nv_bfloat16* h_out,
+    __nv_bfloat16* __restrict__ normed, int64_t T, int d, float eps) {
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const __nv_bfloat16* hr = h + row * d;
+  const __nv_bfloat16* er = e + row * d;
+  __nv_bfloat16* hor = h_out + row * d;
+  float ss = 0.f;
+  for (int i = lane * 8; i < d; i += 256) {
+    const uint4 hv = *reinterpret_cast<const uint4*>(hr + i);
+    const uint4 ev = *reinterpret_cast<const uint4*>(er + i);
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, ew[4] = {ev.x, ev.y, ev.z, ev.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 hf = unpack_bf16x2(hw[t]), ef = unpack_bf16x2(ew[t]);
+      float v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int f = i + 2 * t + u;
+        const float ldt = log_dt[f];
+        const float dt = ldt > 20.f ? ldt : (ldt < -20.f ? expf(ldt) : log1pf(expf(ldt)));
+        const float decay = expf(-dt * expf(log_A[f]));
+        v[u] = decay * (u ? hf.y : hf.x) + dt * (u ? ef.y : ef.x);
+      }
+      o[t] = pack_bf16x2(v[0], v[1]);
+      const float2 r = unpack_bf16x2(o[t]);  // the stored (rounded) values feed the norm
+      ss = fmaf(r.x, r.x, ss);
+      ss = fmaf(r.y, r.y, ss);
+    }
+    *reinterpret_cast<uint4*>(hor + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / float(d) + eps);
+  __nv_bfloat16* nr = normed + row * d;
+  for (int i = lane * 8; i < d; i += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(hor + i);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gain + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t g[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 f = unpack_bf16x2(w[t]);
+      const float2 sc = unpack_bf16x2(g[t]);
+      o[t] = pack_bf16x2(f.x * inv * sc.x, f.y * inv * sc.y);
+    }
+    *reinterpret_cast<uint4*>(nr + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d, float eps, cudaStream_t s) {
   if (T == 0) return BELL_OK;
   const int64_t blocks = (T + 7) / 8;
@@ -106,6 +165,24 @@ int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gai
   if (!aligned16(x) || !aligned16(gain) || !aligned16(out)) return fail(BELL_ERR_ALIGN, "bell_rmsnorm_bf16: alignment");
   if (int rc = require_sm100()) return rc;
   return launch_rmsnorm(x, gain, out, T, d_model, eps, static_cast<cudaStream_t>(stream));
+}
+
+int bell_inject_rmsnorm_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,
+                             const float* log_dt, const void* gain, float eps, void* h_out, void* normed,
+                             void* stream) {
+  if (!h || !e || !log_A || !log_dt || !gain || !h_out || !normed)
+    return fail(BELL_ERR_ARG, "bell_inject_rmsnorm_bf16: NULL pointer");
+  if (T < 0 || d_model <= 0 || d_model % 8 != 0)
+    return fail(BELL_ERR_SHAPE, "bell_inject_rmsnorm_bf16: d_model % 8 != 0");
+  if (!aligned16(h) || !aligned16(e) || !aligned16(gain) || !aligned16(h_out) || !aligned16(normed))
+    return fail(BELL_ERR_ALIGN, "bell_inject_rmsnorm_bf16: alignment");
+  if (int rc = require_sm100()) return rc;
+  if (T == 0) return BELL_OK;
+  bell_inject_rmsnorm_kernel<<<unsigned((T + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(e), log_A, log_dt,
+      static_cast<const __nv_bfloat16*>(gain), static_cast<__nv_bfloat16*>(h_out), static_cast<__nv_bfloat16*>(normed),
+      T, d_model, eps);
+  return check_launch("bell_inject_rmsnorm_kernel");
 }
 
 int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,

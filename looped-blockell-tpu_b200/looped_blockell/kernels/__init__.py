@@ -9,8 +9,8 @@ already defined in the process).
 
 from .ops import (TILE_IN_OUT, TILE_OUT_IN, block_ell_linear, block_ell_swiglu_fwd,  # noqa: F401
                   block_ell_swiglu_fwd_with_intermediate, plan_bytes, read_status, rmsnorm)
-from .loop import (diagonal_injection, looped_ffn, persistent_mlp_step, pin_weights_l2,  # noqa: F401
-                   unpin_weights_l2)
+from .loop import (diagonal_injection, inject_rmsnorm, looped_ffn, persistent_mlp_step,  # noqa: F401
+                   pin_weights_l2, unpin_weights_l2)
 from .backward import (block_ell_sddmm, block_ell_swiglu, block_ell_swiglu_bwd, down_silu_bwd,  # noqa: F401
                        silu_mul_bwd, transpose_ell, transposed_topology)
 from .convert import dense_to_block_ell  # noqa: F401

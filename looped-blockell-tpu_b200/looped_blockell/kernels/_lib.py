@@ -103,6 +103,8 @@ SIGNATURES = {
     "bell_loop_fwd_bf16": (C.c_int, [C.POINTER(BellLoopDesc), C.c_void_p]),
     "bell_diag_injection_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                            C.c_void_p, C.c_void_p]),
+    "bell_inject_rmsnorm_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_void_p, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p]),
     "bell_rmsnorm_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
                                     C.c_void_p]),
     "bell_silu_mul_bwd_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

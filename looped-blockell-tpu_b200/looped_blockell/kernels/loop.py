@@ -65,13 +65,32 @@ def diagonal_injection(h, e, log_A, log_dt) -> torch.Tensor:
     return out
 
 
+def inject_rmsnorm(h, e, log_A, log_dt, gain, eps: float = 1e-5):
+    """``(h_inj, RMSNorm(h_inj) * gain)`` in one pass, ``h_inj`` the diagonal
+    injection of ``h`` (bit-identical to ``diagonal_injection`` then
+    ``rmsnorm``)."""
+    _check_cuda("h", h)
+    if h.dtype != torch.bfloat16 or e.dtype != torch.bfloat16 or gain.dtype != torch.bfloat16:
+        raise RuntimeError("inject_rmsnorm: h, e and gain must be bf16")
+    h, e, gain = h.contiguous(), e.contiguous(), gain.contiguous()
+    la, ld = log_A.float().contiguous(), log_dt.float().contiguous()
+    d = h.shape[-1]
+    h_out, normed = torch.empty_like(h), torch.empty_like(h)
+    with torch.cuda.device(h.device):
+        _lib.check(_lib.load().bell_inject_rmsnorm_bf16(h.numel() // d, d, h.data_ptr(), e.data_ptr(), la.data_ptr(),
+                                                        ld.data_ptr(), gain.data_ptr(), float(eps), h_out.data_ptr(),
+                                                        normed.data_ptr(), _stream()), "inject_rmsnorm")
+    return h_out, normed
+
+
 def persistent_mlp_step(h, e, log_A, log_dt, norm_scales: Sequence[torch.Tensor], gate_values, gate_col_idx,
                         up_values, up_col_idx, down_values, down_col_idx, eps: float = 1e-5,
                         layout: int = TILE_IN_OUT) -> torch.Tensor:
     """Reference ``titan::persistent_mlp_step``: injection, then for each of the
-    n_core blocks ``h = h + SwiGLU(RMSNorm(h))`` (persistent_core.cu:273-337).
-    The reference hard-codes eps 1e-6 in CUDA while its JAX/PyTorch models use
-    1e-5 (config.py:110); ``eps`` defaults to the model value."""
+    n_core blocks ``h = h + SwiGLU(RMSNorm(h))`` (persistent_core.cu:273-337),
+    the injection fused with the first RMSNorm.  The reference op hard-codes
+    eps 1e-6 in CUDA while its JAX/PyTorch models use 1e-5 (config.py:110);
+    ``eps`` defaults to the model value and ``torch.ops.titan`` passes 1e-6."""
     from .ops import block_ell_swiglu_fwd
     n = len(norm_scales)
     if n == 0:
@@ -83,9 +102,10 @@ def persistent_mlp_step(h, e, log_A, log_dt, norm_scales: Sequence[torch.Tensor]
         raise RuntimeError(f"persistent_mlp_step: h must be 2D [N, d_model], got shape {tuple(h.shape)}")
     if h.dtype != torch.bfloat16:
         raise RuntimeError("persistent_mlp_step: h must be bf16")
-    cur = diagonal_injection(h, e, log_A, log_dt)
+    cur, normed = inject_rmsnorm(h, e, log_A, log_dt, norm_scales[0].to(torch.bfloat16), eps)
     for i in range(n):
-        normed = rmsnorm(cur, norm_scales[i].to(torch.bfloat16), eps)
+        if i > 0:
+            normed = rmsnorm(cur, norm_scales[i].to(torch.bfloat16), eps)
         from .ops import _swiglu
         cur = _swiglu(normed, gate_values[i], gate_col_idx[i], up_values[i], up_col_idx[i], down_values[i],
                       down_col_idx[i], True, layout, False, residual=cur)[0]

@@ -85,8 +85,9 @@ def _unpin():
 
 def _step_cuda(h, e, log_A, log_dt, norm_scales, gate_values, gate_col_idx, up_values, up_col_idx, down_values,
                down_col_idx):
+    # the reference op's RMSNorm eps (persistent_core.cu:317)
     return _loop.persistent_mlp_step(h, e, log_A, log_dt, norm_scales, gate_values, gate_col_idx, up_values,
-                                     up_col_idx, down_values, down_col_idx, layout=_ops.TILE_OUT_IN)
+                                     up_col_idx, down_values, down_col_idx, eps=1e-6, layout=_ops.TILE_OUT_IN)
 
 
 def _step_meta(h, e, log_A, log_dt, norm_scales, gate_values, gate_col_idx, up_values, up_col_idx, down_values,
