@@ -68,3 +68,26 @@ def test_layer_create_from_dense_uses_the_kernel_and_runs_forward():
     y = block_ell_matmul(x, be)
     ref = O.block_ell_matmul(x.float().cpu().numpy().astype(np.float64), ov, oc)
     assert O.rel_l2(y.float().cpu().numpy(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("density", [None, 0.5])
+def test_swiglu_from_state_dict_on_gpu_runs_the_forward(density):
+    from looped_blockell import interop
+    K = _K()
+    rng = np.random.default_rng(11)
+    d, F, B, T = 256, 512, 64, 130
+    sd = {f"mlp.{k}.weight": torch.from_numpy((rng.standard_normal(s) * 0.05).astype(np.float32)).cuda()
+          for k, s in (("w_gate", (F, d)), ("w_up", (F, d)), ("w_down", (d, F)))}
+    w = interop.swiglu_from_state_dict(sd, "mlp.", tile_size=B, density=density)
+    x = torch.from_numpy(rng.standard_normal((T, d)).astype(np.float32)).to(torch.bfloat16).cuda()
+    out = K.block_ell_swiglu_fwd(x, w["vg"], w["cg"], w["vu"], w["cu"], w["vd"], w["cd"])
+    torch.cuda.synchronize()
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    ref = O.swiglu_ffn(f(x), (f(w["vg"]), w["cg"].cpu().numpy(), 0), (f(w["vu"]), w["cu"].cpu().numpy(), 0),
+                       (f(w["vd"]), w["cd"].cpu().numpy(), 0))
+    assert O.rel_l2(f(out), ref) < 1e-2
+    if density is None:  # every tile kept: the dense MLP of the (bf16) weights
+        Wg, Wu, Wd = (f(sd[f"mlp.{k}.weight"].to(torch.bfloat16)) for k in ("w_gate", "w_up", "w_down"))
+        g = f(x) @ Wg.T
+        dense = (g / (1 + np.exp(-g)) * (f(x) @ Wu.T)) @ Wd.T
+        assert O.rel_l2(f(out), dense) < 1e-2
