@@ -30,6 +30,7 @@ static constexpr int kW = kB * kB;   // unpacked int8 weight tile bytes (4 KB)
 static constexpr int kP = kB * kB / 4;  // packed 2-bit weight tile bytes (1 KB)
 static constexpr int kStage = kA + kW + kP;  // 13 KB, 1024-aligned
 static constexpr int kNS = 12;
+static_assert(kNS % 4 == 0, "each stage keeps one unpack warp");
 static constexpr int kSlots = 8;     // TMEM result slots of 64 columns
 static constexpr int kEpiWarps = 16; // 4 per TMEM lane quadrant, 16 result columns each
 static constexpr int kEpiCols = kB / (kEpiWarps / 4);
@@ -121,7 +122,7 @@ struct TernParams {
 
 // Warp roles: 0 TMA producer (activation tile and packed weight tile of each
 // step, into the stage), 1 TMEM owner + MMA issuer, 2-5 weight unpackers
-// (packed tile in shared memory -> int8 tile), 6-21 epilogue (four warps per
+// (packed tile in shared memory -> int8 tile, alternate steps), 6-21 epilogue (four warps per
 // TMEM lane quadrant, each owning 16 of the 64 result columns).  Every plan step is one (column
 // block, weight tile) pair of ONE matrix; results land in one of 8 TMEM slots
 // of 64 int32 columns and are consumed in plan order.
@@ -248,40 +249,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp < 6) {
     // ------------------------------------------------------- weight unpack
-    // The producer copied the stage's packed tile next to it (pfull); the
-    // group expands it into the int8 tile the MMA reads.
-    const int t = threadIdx.x - 64;  // 0..127
+    // The producer copied the stage's packed tile next to it (pfull); an
+    // unpack warp expands it into the int8 tile the MMA reads.  The four
+    // warps take alternate steps (step g -> warp g % 4; kNS is a multiple of
+    // 4, so every stage always has the same single waiter), so four tiles
+    // are expanded at once instead of one tile by the whole group.
+    const int uw = warp - 2;
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    uint32_t g = 0;
+    bool alive = true;
+    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
       const int r = u % p.R;
       const int n = p.counts[r] & 0xFFFF;
-      bool alive = true;
-      for (int s = 0; s < n; ++s) {
-        mbar_wait(&pfull[stage], phase, ctl);
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // one abort decision for the whole group
-        if (*abort_flag) {
-          alive = false;
-          break;
-        }
-        uint8_t* w = smem + stage * kStage + kA;
-        const uint32_t* packed = reinterpret_cast<const uint32_t*>(w + kW);
+      for (int s = 0; s < n; ++s, ++g) {
+        if (int(g & 3u) == uw) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&pfull[stage], phase, ctl))) {
+            alive = false;
+            break;
+          }
+          uint8_t* w = smem + stage * kStage + kA;
+          const uint32_t* packed = reinterpret_cast<const uint32_t*>(w + kW);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {  // 256 words per tile, 2 per thread
-          const int widx = t + i * 128;
-          const int nrow = widx >> 2, c = widx & 3;
-          const uint32_t word = packed[widx];
-          *reinterpret_cast<uint4*>(w + nrow * 64 + ((c ^ ((nrow >> 1) & 3)) << 4)) = unpack16(word);
+          for (int i = 0; i < 8; ++i) {  // 256 words per tile, 8 per lane
+            const int widx = lane + i * 32;
+            const int nrow = widx >> 2, c = widx & 3;
+            const uint32_t word = packed[widx];
+            *reinterpret_cast<uint4*>(w + nrow * 64 + ((c ^ ((nrow >> 1) & 3)) << 4)) = unpack16(word);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[stage]);
         }
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (t == 0) mbar_arrive(&full[stage]);
         if (++stage == kNS) {
           stage = 0;
           phase ^= 1;
         }
       }
-      if (!alive) break;
     }
   } else {
     // ------------------------------------------------------------ epilogue
