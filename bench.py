@@ -599,6 +599,7 @@ def run_gpu(args, cfg, rank, world):
             line["roofline"] = {"bound": "tensor", "kernel": "gate/up kernel (bell_bf16_fmajor_kernel at B=128, "
                                 "bell_bf16_kernel at B=64)", "achieved": gu["tflops"],
                                 "peak": tc_peak, "unit": "TFLOP/s", "frac": gu["tflops"] / tc_peak,
+                                "frac_of_sustained": gu["tflops"] / tc_sust,
                                 "peak_source": f"{peak_src} bf16 burst", "traffic": traffic,
                                 "traffic_source": GU_DRAM_NOTE.get(args.config) if traffic else None,
                                 "kernel_ms": gu["ms"], "whole_step_frac": tflops / world / tc_peak}

@@ -35,7 +35,8 @@ static constexpr int kSlots = 8;     // TMEM result slots of 64 columns
 static constexpr int kEpiWarps = 16; // 4 per TMEM lane quadrant, 16 result columns each
 static constexpr int kEpiCols = kB / (kEpiWarps / 4);
 static constexpr int kThreads = 32 * (6 + kEpiWarps);  // 22 warps
-static constexpr int kSmem = kNS * kStage + 1024 + 1024 + kEpiWarps * kRowMax * 4;
+// stages, barriers, per-epilogue-warp scale rows, the producer's plan row
+static constexpr int kSmem = kNS * kStage + 1024 + 1024 + kEpiWarps * kRowMax * 4 + kRowMax * 4;
 
 // ------------------------------------------------------------ quantisation
 
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = tempty + kSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   float* epi_scales = reinterpret_cast<float*>(smem + kNS * kStage + 1024);  // [epilogue warp][kRowMax]
+  uint32_t* prod_row = reinterpret_cast<uint32_t*>(epi_scales + kEpiWarps * kRowMax);  // [kRowMax]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   Ctl ctl{abort_flag, p.status, p.timeout_ns};
@@ -168,18 +170,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_units = p.n_mtiles * p.R;
 
   if (warp == 0) {
-    if (lane == 0) {  // -------------------------------------------- producer
-      prefetch_tmap(&tm_a);
-      const uint64_t pol = policy_evict_normal();
-      const uint64_t pol_w = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      bool alive = true;
-      for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
-        const int m = u / p.R, r = u % p.R;
-        const int n = p.counts[r] & 0xFFFF;
+    // --------------------------------------------------------------- producer
+    // The warp fetches each unit's plan row one unit ahead (bell_sched.cuh);
+    // lane 0 issues the copies, reading its steps from shared memory.
+    if (lane == 0) prefetch_tmap(&tm_a);
+    const uint64_t pol = policy_evict_normal();
+    const uint64_t pol_w = policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    bool alive = true;
+    RowAhead ahead;
+    if (int(blockIdx.x) < n_units) row_fetch(ahead, p.plan, p.counts, p.S, int(blockIdx.x) % p.R);
+    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+      const int m = u / p.R, r = u % p.R;
+      const int n = ahead.cnt & 0xFFFF;
+      __syncwarp();
+      row_put(ahead, prod_row, p.S);
+      __syncwarp();
+      if (u + int(gridDim.x) < n_units) row_fetch(ahead, p.plan, p.counts, p.S, (u + int(gridDim.x)) % p.R);
+      if (lane == 0) {
         for (int s = 0; s < n; ++s) {
-          const uint32_t e = p.plan[size_t(r) * p.S + s];
+          const uint32_t e = prod_row[s];
           const int c = int(e & 0xFFFFu);
           const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
           const uint8_t* src = (k0 != 255u) ? p.packed0 + (size_t(r) * p.K0 + k0) * kP
@@ -199,6 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      alive = __shfl_sync(0xffffffffu, alive, 0);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer
