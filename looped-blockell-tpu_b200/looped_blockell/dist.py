@@ -94,29 +94,44 @@ class ShardedSwiGLU:
         return t
 
     def forward(self, x: torch.Tensor, out: torch.Tensor = None, add_residual: bool = True) -> torch.Tensor:
-        import torch.distributed as dist
+        """This rank's token slice of the full forward (bf16, CUDA)."""
         from .kernels.ops import block_ell_gate_up, block_ell_linear
+        T = x.shape[0]
+        Tc = T // pick_chunks(T, self.world, self.want_chunks)
+        h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, x.device)
+
+        def partial_fn(xi: torch.Tensor, dst: torch.Tensor) -> None:
+            block_ell_gate_up(xi, self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h)
+            block_ell_linear(h, self.vd, self.cd, out=dst)
+
+        return self.run_chunks(x, partial_fn, out, add_residual)
+
+    def run_chunks(self, x: torch.Tensor, partial_fn, out: torch.Tensor = None, add_residual: bool = True,
+                   dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """The chunk pipeline of ``forward`` around any partial computation:
+        ``partial_fn(x_chunk, dst)`` writes this rank's partial ``[Tc, d_model]``
+        for a token chunk; the reduce-scatter of chunk i runs (async) while
+        chunk i+1 computes, two partial buffers alternate, and the residual is
+        added on the owned rows at the end."""
+        import torch.distributed as dist
         T = x.shape[0]
         n = pick_chunks(T, self.world, self.want_chunks)
         Tc = T // n
         per = Tc // self.world
         if out is None:
-            out = self.alloc_out(T, x)
-        dev = x.device
-        h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, dev)
-        partial = [self._buf(f"p{i % 2}", (Tc, self.d_model), torch.bfloat16, dev) for i in range(n)]
+            out = torch.empty((T // self.world, self.d_model), dtype=dtype, device=x.device)
+        partial = [self._buf(f"p{i % 2}", (Tc, self.d_model), dtype, x.device) for i in range(n)]
         works = []
         for i in range(n):
             xi = x[i * Tc:(i + 1) * Tc]
             if i >= 2:
                 works[i - 2].wait()  # partial buffer i%2 is free again
-            block_ell_gate_up(xi, self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h)
-            block_ell_linear(h, self.vd, self.cd, out=partial[i])
+            partial_fn(xi, partial[i])
             works.append(dist.reduce_scatter_tensor(out[i * per:(i + 1) * per], partial[i], op=dist.ReduceOp.SUM,
                                                     group=self.group, async_op=True))
         for w in works:
             w.wait()
         if add_residual:
-            rows = owned_rows(T, self.rank, self.world, n).to(dev)
-            out.add_(x.index_select(0, rows))
+            rows = owned_rows(T, self.rank, self.world, n).to(x.device)
+            out.add_(x.index_select(0, rows).to(out.dtype))
         return out

@@ -1,8 +1,9 @@
 """Host-side logic of the d_ff-sharded forward, on CPU: shard ranges, down-ELL
-repacking, token ownership after the chunked reduce-scatter, and a
-world_size-2 gloo run where each rank computes its partial with the oracle
-and the ranks sum them (gloo has no reduce-scatter, so all_reduce + the
-ownership map stands in for it)."""
+repacking, token ownership after the chunked reduce-scatter, a world_size-2
+gloo run where each rank computes its partial with the oracle and the ranks
+sum them (all_reduce + the ownership map), and the chunked reduce-scatter
+pipeline itself (``ShardedSwiGLU.run_chunks``) on gloo at world sizes 2 and 4
+with oracle partials."""
 
 import os
 import socket
@@ -96,3 +97,46 @@ def test_gloo_two_ranks_reconstruct_output():
     for p in procs:
         p.join(timeout=60)
     assert all(err < 1e-12 for _, err in res), res
+
+
+def _chunk_worker(rank, world, port, c, full, q):
+    """The chunked reduce-scatter pipeline of ShardedSwiGLU (run_chunks) on
+    gloo, with this rank's partials from the oracle."""
+    from looped_blockell.dist import ShardedSwiGLU
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in c.items() if k != "B"}
+    model = ShardedSwiGLU(t["vg"], t["cg"], t["vu"], t["cu"], t["vd"], t["cd"], rank, world, chunks=4)
+    cl = {k: v for k, v in c.items()}
+    lo, hi = model.lo, model.hi
+
+    def partial_fn(xi, dst):
+        sub = dict(cl, x=xi.numpy())
+        dst.copy_(torch.from_numpy(_partial(sub, lo, hi)))
+
+    x = torch.from_numpy(c["x"])
+    out = model.run_chunks(x, partial_fn, dtype=torch.float64)
+    n = pick_chunks(x.shape[0], world, 4)
+    rows = owned_rows(x.shape[0], rank, world, n)
+    q.put((rank, n, O.rel_l2(out.numpy(), full[rows.numpy()])))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_chunked_reduce_scatter_reconstructs_output(world):
+    c = _case(seed=21 + world, T=4 * world * 128)
+    full = O.swiglu_ffn(c["x"], (c["vg"], c["cg"], 0), (c["vu"], c["cu"], 0), (c["vd"], c["cd"], 0),
+                        add_residual=True)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_chunk_worker, args=(r, world, port, c, full, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(n == 4 for _, n, _ in res), res
+    assert all(err < 1e-12 for _, _, err in res), res
