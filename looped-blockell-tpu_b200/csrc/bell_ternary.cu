@@ -121,6 +121,46 @@ struct TernParams {
   uint64_t timeout_ns;
 };
 
+// Two fp32 lanes in one 64-bit register pair, for the sm_100 paired fp32
+// instructions; each lane rounds exactly as the scalar IEEE operation.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// acc[j] += s * float(I[2j .. 2j+1]) for 8 pairs, exactly rounded: the int32
+// tile sums (|I| < 2^22) become floats through the 2^23 + 2^22 bias trick
+// (paired subtract), the products are scalar round-to-nearest multiplies and
+// the sums paired adds.  A paired multiply feeding a paired add measured as
+// fused (one rounding) on sm_100 even with .rn, so the multiply stays scalar
+// (mul.rn is never contracted).
+__device__ __forceinline__ void scale_add16(uint64_t (&acc)[8], const uint32_t (&v)[16], float s) {
+  const uint64_t bias2 = f2_pack(12582912.0f, 12582912.0f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 fi = f2_unpack(f2_sub_rn(f2_pack(__int_as_float(int(v[2 * j]) + 0x4B400000),
+                                                  __int_as_float(int(v[2 * j + 1]) + 0x4B400000)),
+                                          bias2));
+    acc[j] = f2_add_rn(acc[j], f2_pack(__fmul_rn(s, fi.x), __fmul_rn(s, fi.y)));
+  }
+}
+
 // Warp roles: 0 TMA producer (activation tile and packed weight tile of each
 // step, into the stage), 1 TMEM owner + MMA issuer, 2-5 weight unpackers
 // (packed tile in shared memory -> int8 tile, alternate steps), 6-21 epilogue (four warps per
@@ -339,9 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 32 * kAhead + lane; j < n; j += 32) wsc[j] = step_scale(r, j);
       __syncwarp();
       if (u + int(gridDim.x) < n_units) fetch(u + gridDim.x);
-      float acc0[kEpiCols], acc1[kEpiCols];
+      static_assert(kEpiCols == 16, "scale_add16 covers 16 columns");
+      uint64_t acc0p[8], acc1p[8];  // gate / up (or the single matrix) as fp32 pairs
 #pragma unroll
-      for (int j = 0; j < kEpiCols; ++j) acc0[j] = acc1[j] = 0.f;
+      for (int j = 0; j < 8; ++j) acc0p[j] = acc1p[j] = 0ull;
       bool alive = true;
       for (int s = 0; s < n; ++s) {
         const float ss = wsc[s];
@@ -358,20 +399,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);
-#pragma unroll
-        for (int j = 0; j < kEpiCols; ++j) {
-          // exact int32 -> fp32 for |I| < 2^22 (here |I| <= 128 * 64)
-          const float fi = __fsub_rn(__int_as_float(int(v[j]) + 0x4B400000), 12582912.0f);
-          const float prod = __fmul_rn(sc, fi);
-          if (!GU || is0) acc0[j] = __fadd_rn(acc0[j], prod);
-          else acc1[j] = __fadd_rn(acc1[j], prod);
-        }
+        // |I| <= 128 * 64 < 2^22; the step's matrix is warp-uniform
+        if (!GU || is0) scale_add16(acc0p, v, sc);
+        else scale_add16(acc1p, v, sc);
         if (++slot == kSlots) {
           slot = 0;
           sphase ^= 1;
         }
       }
       if (!alive) break;
+      float acc0[kEpiCols], acc1[kEpiCols];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 a = f2_unpack(acc0p[j]), b = f2_unpack(acc1p[j]);
+        acc0[2 * j] = a.x;
+        acc0[2 * j + 1] = a.y;
+        acc1[2 * j] = b.x;
+        acc1[2 * j + 1] = b.y;
+      }
       const int64_t row = int64_t(m) * kBM + q * 32 + lane;
       if (row < p.T) {
         const float ts = p.tok_scale[row];
