@@ -11,10 +11,11 @@
 //   * bell_sddmm_kernel: the tile gradients d_W[r, k] = a[:, c]^T b[:, r]
 //     summed over tokens (swiglu_bwd.cu:13-14, 29-30), on tcgen05 with the
 //     token dimension as the MMA K and both operands MN-major straight from
-//     the row-major activations.  A work unit is two slots of one block-row:
-//     at tile size 64 the two slots' a features form M = 128 against the
-//     row's 64 b features; at 128 the row's b features are M and the two
-//     slots' a features N = 256, so one b chunk serves both slots.  Tokens
+//     the row-major activations.  At tile size 64 a work unit is four slots
+//     of one block-row in two accumulators (two slots' a features form
+//     M = 128 against the row's 64 b features); at 128 it is two slots, the
+//     row's b features M and the two slots' a features N = 256.  Either way
+//     one b chunk serves every slot of the unit.  Tokens
 //     run in ranges sized to stay in L2; each CTA takes an equal share of a
 //     range and adds its fp32 partial tiles into the gradient with atomics.
 #include <string>
@@ -68,23 +69,27 @@ __global__ void __launch_bounds__(256) bell_f32_to_bf16_kernel(const float* __re
 static constexpr int kTok = 64;   // tokens per stage (MMA K per stage)
 static constexpr int kThr = 192;  // warp 0 producer, 1 MMA, 2-5 epilogue
 
-// A unit is two slots of one block-row.  B = 64: M = the two slots' a
-// features (2 x 64), N = the row's 64 b features.  B = 128 (TR): M = the
-// row's 128 b features, N = the two slots' a features (2 x 128), so the b
-// chunk is loaded once for both slots.  Both operands are MN-major straight
-// from the row-major activations: 64-token x 64-feature boxes, 128-byte
-// swizzle, 64-feature groups 8 KB apart.
+// B = 64: a unit is four slots of one block-row in two accumulators; each
+// accumulator's M is two slots' a features (2 x 64) against the row's 64 b
+// features (N), so one b chunk serves four slots.  B = 128 (TR): a unit is
+// two slots; M = the row's 128 b features, N = the two slots' a features
+// (2 x 128).  Both operands are MN-major straight from the row-major
+// activations: 64-token x 64-feature boxes, 128-byte swizzle, 64-feature
+// groups 8 KB apart.
 template <int B>
 struct SCfg {
   static constexpr bool TR = B == 128;
-  static constexpr int SLOTS = 2;
-  static constexpr int A_BYTES = 16384;                // B=64: two a slots; B=128: b
+  static constexpr int SLOTS = TR ? 2 : 4;
+  static constexpr int NACC = TR ? 1 : 2;              // accumulators per unit
+  static constexpr int SLOT_BYTES = TR ? 16384 : 8192; // one slot's a chunk
+  static constexpr int A_BYTES = TR ? 16384 : 32768;   // B=64: four a slots; B=128: b
   static constexpr int B_BYTES = TR ? 32768 : 8192;    // B=64: b; B=128: two a slots
-  static constexpr int STAGE = A_BYTES + B_BYTES;      // 24 / 48 KB
+  static constexpr int STAGE = A_BYTES + B_BYTES;      // 40 / 48 KB
   static constexpr int N = TR ? 256 : 64;              // MMA N = accumulator columns
-  static constexpr int NS = 196608 / STAGE;            // 8 / 4 stages
+  static constexpr int NS = 196608 / STAGE;            // 4 / 4 stages
   static constexpr int SMEM = NS * STAGE + 1024 + 512;
-  static constexpr int TMEM_COLS = 2 * N;              // two accumulators
+  static constexpr int TMEM_COLS = 2 * NACC * N;       // double-buffered unit accumulators
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation");
 };
 
 struct SddmmParams {
@@ -105,10 +110,16 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 }
 
 struct Unit {
-  int r, k0, k1, c0, c1;
+  int r;
+  int k[4], c[4];    // slot and validated column (-1: absent or dead) of each slot of the unit
   int64_t ch0, ch1;  // 64-token chunks [ch0, ch1)
   bool any;
 };
+
+// a[i] with a runtime i, by selects (keeps the unit in registers)
+__device__ __forceinline__ int pick4(const int (&a)[4], int i) {
+  return i == 0 ? a[0] : i == 1 ? a[1] : i == 2 ? a[2] : a[3];
+}
 
 template <int SLOTS>
 __device__ __forceinline__ Unit unit_of(int u, const SddmmParams& p) {
@@ -116,17 +127,20 @@ __device__ __forceinline__ Unit unit_of(int u, const SddmmParams& p) {
   const int per = p.R * p.KP;
   const int s = u / per, rem = u - s * per;
   x.r = rem / p.KP;
-  const int kp = rem - x.r * p.KP;
-  x.k0 = kp * SLOTS;
-  x.k1 = (SLOTS == 2 && x.k0 + 1 < p.K) ? x.k0 + 1 : -1;
-  const int c0 = p.cols[size_t(x.r) * p.K + x.k0];
-  const int c1 = x.k1 >= 0 ? p.cols[size_t(x.r) * p.K + x.k1] : -1;
-  x.c0 = (c0 >= 0 && c0 < p.C) ? c0 : -1;
-  x.c1 = (c1 >= 0 && c1 < p.C) ? c1 : -1;
+  const int k0 = (rem - x.r * p.KP) * SLOTS;
+  bool live = false;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = (j < SLOTS && k0 + j < p.K) ? k0 + j : -1;
+    const int c = k >= 0 ? p.cols[size_t(x.r) * p.K + k] : -1;
+    x.k[j] = k;
+    x.c[j] = (c >= 0 && c < p.C) ? c : -1;
+    live |= x.c[j] >= 0;
+  }
   const int64_t total = (p.T + kTok - 1) / kTok;
   x.ch0 = int64_t(s) * p.split_chunks;
   x.ch1 = x.ch0 + p.split_chunks < total ? x.ch0 + p.split_chunks : total;
-  x.any = (x.c0 >= 0 || x.c1 >= 0) && x.ch1 > x.ch0;
+  x.any = live && x.ch1 > x.ch0;
   return x;
 }
 
@@ -231,8 +245,8 @@ __global__ void __launch_bounds__(kThr, 1)
         if (head) {  // once per unit: report indices outside [-1, C)
 #pragma unroll
           for (int j = 0; j < SLOTS; ++j) {
-            const int k = x.k0 + j;
-            if (k < p.K) {
+            const int k = x.k[j];
+            if (k >= 0) {
               const int c = p.cols[size_t(x.r) * p.K + k];
               if (c < -1 || c >= p.C) atomicOr(p.status, BELL_STATUS_COLIDX);
             }
@@ -246,19 +260,20 @@ __global__ void __launch_bounds__(kThr, 1)
           }
           uint8_t* st = smem + stage * C::STAGE;
           const int y = int(ch * kTok);
-          constexpr uint32_t SLOT_BYTES = C::TR ? 16384 : 8192;  // one slot's a chunk
-          const uint32_t bytes = (C::TR ? 16384 : 8192) + (x.c0 >= 0 ? SLOT_BYTES : 0) + (x.c1 >= 0 ? SLOT_BYTES : 0);
+          uint32_t bytes = C::TR ? 16384 : 8192;  // the b chunk
+#pragma unroll
+          for (int j = 0; j < SLOTS; ++j) bytes += x.c[j] >= 0 ? C::SLOT_BYTES : 0;
           mbar_arrive_expect_tx(&full[stage], bytes);
-          // a slots: B=64 -> A operand groups 0 / 1; B=128 -> B operand, 16 KB each
+          // a slots: B=64 -> A operand, 8 KB each; B=128 -> B operand, 16 KB each
           uint8_t* a_dst = st + (C::TR ? C::A_BYTES : 0);
           uint8_t* b_dst = st + (C::TR ? 0 : C::A_BYTES);
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int c = j == 0 ? x.c0 : x.c1;
+          for (int j = 0; j < SLOTS; ++j) {
+            const int c = x.c[j];
             if (c < 0) continue;
 #pragma unroll
             for (int h = 0; h < B / 64; ++h)
-              tma_load_2d(a_dst + j * SLOT_BYTES + h * 8192, &tm_a, &full[stage], c * B + h * 64, y, pol);
+              tma_load_2d(a_dst + j * C::SLOT_BYTES + h * 8192, &tm_a, &full[stage], c * B + h * 64, y, pol);
           }
 #pragma unroll
           for (int h = 0; h < B / 64; ++h)
@@ -305,7 +320,7 @@ __global__ void __launch_bounds__(kThr, 1)
       ++i;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl))) break;
       tc_fence_after();
-      const uint32_t d = tmem + uint32_t(buf * C::N);
+      const uint32_t d = tmem + uint32_t(buf * C::NACC * C::N);
       bool ok = true;
       for (int64_t ch = a0; ch < a1; ++ch) {
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, ctl))) {
@@ -317,8 +332,12 @@ __global__ void __launch_bounds__(kThr, 1)
         const uint64_t bd = b_desc0 + uint64_t(stage) * (C::STAGE >> 4);
         if (leader) {
 #pragma unroll
-          for (int kk = 0; kk < kTok / 16; ++kk)
-            mma_bf16(d, ad + kk * (2048 >> 4), bd + kk * (2048 >> 4), IDESC, (ch > a0 || kk > 0) ? 1u : 0u);
+          for (int ac = 0; ac < C::NACC; ++ac) {  // accumulator ac: slots 2ac, 2ac+1 (B=64)
+#pragma unroll
+            for (int kk = 0; kk < kTok / 16; ++kk)
+              mma_bf16(d + uint32_t(ac * C::N), ad + uint64_t(ac) * (16384 >> 4) + kk * (2048 >> 4),
+                       bd + kk * (2048 >> 4), IDESC, (ch > a0 || kk > 0) ? 1u : 0u);
+          }
           mma_commit(&empty[stage]);
         }
         __syncwarp();
@@ -356,18 +375,19 @@ __global__ void __launch_bounds__(kThr, 1)
       ++i;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1u, ctl))) break;
       tc_fence_after();
-      const uint32_t tb = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * C::N);
+      const uint32_t tb = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * C::NACC * C::N);
       if constexpr (!C::TR) {
-        // B = 64: accumulator row = a feature; rows 0-63 slot k0, 64-127 slot k1;
-        // columns = the row's 64 b (output) features
-        const int k = q >= 2 ? x.k1 : x.k0;
-        const int c = q >= 2 ? x.c1 : x.c0;
+        // B = 64: accumulator ac, row = a feature; rows 0-63 slot 2ac, 64-127
+        // slot 2ac+1; columns = the row's 64 b (output) features
         const int fin = row & 63;
-        float* tile = p.grad + (size_t(x.r) * p.K + (k >= 0 ? k : 0)) * B * B;
 #pragma unroll 1
-        for (int j = 0; j < B / 32; ++j) {
+        for (int jj = 0; jj < C::NACC * (B / 32); ++jj) {
+          const int ac = jj / (B / 32), j = jj % (B / 32);
+          const int sl = 2 * ac + (q >= 2 ? 1 : 0);
+          const int k = pick4(x.k, sl), c = pick4(x.c, sl);
+          float* tile = p.grad + (size_t(x.r) * p.K + (k >= 0 ? k : 0)) * B * B;
           uint32_t v[32];
-          tmem_ld32_sync(tb + j * 32, v);
+          tmem_ld32_sync(tb + uint32_t(ac * C::N) + j * 32, v);
           if (c < 0) continue;
           if (!p.out_in) {  // [B_in, B_out]: this row's 32 outputs are contiguous
             float* dst = tile + size_t(fin) * B + j * 32;
@@ -385,8 +405,8 @@ __global__ void __launch_bounds__(kThr, 1)
         // slot k0's a (input) features, 128-255 slot k1's
 #pragma unroll 1
         for (int sl = 0; sl < 2; ++sl) {
-          const int k = sl ? x.k1 : x.k0;
-          const int c = sl ? x.c1 : x.c0;
+          const int k = pick4(x.k, sl);
+          const int c = pick4(x.c, sl);
           if (c < 0) continue;  // warp-uniform
           float* tile = p.grad + (size_t(x.r) * p.K + k) * B * B;
 #pragma unroll 1

@@ -188,3 +188,28 @@ def _same_grads(a, b):
     for x, y in zip(a[1:], b[1:]):
         xf, yf = x.float(), y.float()
         assert torch.all((xf - yf).abs() <= yf.abs() * 2.0 ** -7 + 1e-6)
+
+
+@pytest.mark.parametrize("B", [64, 128])
+def test_swiglu_backward_dead_rows_and_unused_columns(B):
+    """Block-rows whose gate (or down) slots are all dead, and d_ff columns no
+    down slot uses: their gradients are exactly zero, the rest match."""
+    K = _K()
+    T, d, F = 200, 2 * B * 2, 4 * B * 2
+    c = make_case(T, d, F, B, 2, 2, 3, seed=B + 7)
+    c["cg"][1, :] = -1          # gate block-row 1 entirely dead
+    c["cd"][0, :] = -1          # down block-row 0 entirely dead
+    dv = to_dev(c, torch.bfloat16)
+    g = torch.Generator().manual_seed(3)
+    dy = torch.randn(T, d, generator=g).to(torch.bfloat16).cuda()
+    out, h, gp, up = K.block_ell_swiglu_fwd_with_intermediate(dv["x"], dv["vg"], dv["cg"], dv["vu"], dv["cu"],
+                                                              dv["vd"], dv["cd"], add_residual=True)
+    res = K.block_ell_swiglu_bwd(dy, dv["x"], gp, up, h, dv["vg"], dv["cg"], dv["vu"], dv["cu"], dv["vd"], dv["cd"])
+    torch.cuda.synchronize()
+    assert K.read_status() == 0
+    mats = [(_f64(dv[v]), dv[ci].cpu().numpy(), 0) for v, ci in (("vg", "cg"), ("vu", "cu"), ("vd", "cd"))]
+    ref = O.swiglu_ffn_backward(_f64(dv["x"]), *mats, _f64(dy), add_residual=True)
+    for name, a, b in zip(("dx", "d_vg", "d_vu", "d_vd"), res, ref):
+        assert O.rel_l2(_f64(a), b) < TOL, name
+    assert float(res[1][1].float().abs().max()) == 0.0
+    assert float(res[3][0].float().abs().max()) == 0.0
