@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
       break;
     }
     case eng::kEpilogue:
-      eng::epilogue<B, GU, G, SB>(p, s, tmem, 0, ctl);
+      eng::epilogue<B, GU, G, SB>(p, s, tmem, 0, ctl, SB ? &tm_w1 : nullptr);  // SB: tm_w1 maps the output
       break;
   }
   eng::teardown<G>(tmem);
@@ -747,10 +747,16 @@ int bell_down_silu_bwd_bf16(const BellDownBwdDesc* d, void* stream) {
   p.status = status;
   p.timeout_ns = wait_budget_ns();
   // token-major engine at both tile sizes: its epilogue owns whole token
-  // rows, so the gate/up rows are staged with 16-byte copies
+  // rows, so the gate/up rows are staged with 16-byte copies; at B = 64 the
+  // results leave through TMA stores (the third map, unused by a linear)
   const bool mn = w.layout == BELL_TILE_IN_OUT;
-  if (w.B == 64)
-    return mn ? launch_bf16<64, false, true, true>(ma, mw, mw, p, s) : launch_bf16<64, false, false, true>(ma, mw, mw, p, s);
+  if (w.B == 64) {
+    CUtensorMap mo;
+    if (int rc = make_map_2d(&mo, d->d_gate_up, MapType::BF16, uint64_t(2 * F), uint64_t(d->T), uint64_t(2 * F) * 2,
+                             64, 32, Swz::B128))
+      return rc;
+    return mn ? launch_bf16<64, false, true, true>(ma, mw, mo, p, s) : launch_bf16<64, false, false, true>(ma, mw, mo, p, s);
+  }
   return mn ? launch_bf16<128, false, true, true>(ma, mw, mw, p, s) : launch_bf16<128, false, false, true>(ma, mw, mw, p, s);
 }
 

@@ -58,7 +58,9 @@ struct Geo {
   static constexpr int NBUF = 4 * ACC_COLS <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = 2 * NBUF * ACC_COLS < 128 ? 128 : 2 * NBUF * ACC_COLS;
   // align + barriers (512) + stage info (64) + one staged plan row per producer
-  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + 576 + kProds * kRowMax * 4 + EPI_BYTES;
+  // the staging area starts 1024-aligned (its slots are 128-byte-swizzled TMA boxes at B = 64)
+  static constexpr int EPI_OFF = ((576 + kProds * kRowMax * 4) + 1023) & ~1023;
+  static constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 + EPI_OFF + EPI_BYTES;
   // the two producers of a ring take alternate steps; with one stage per
   // ring a producer could wait on a phase two ahead of the stage (parity
   // aliasing), so each ring needs at least two stages
@@ -76,7 +78,7 @@ struct Smem {
   volatile int* abort_flag;
   uint32_t* stage_info;            // [ring * NR + stage]
   uint32_t* rows;                  // [producer][kRowMax]
-  uint8_t* epi;                    // SB: [epilogue warp][slot][gate | up rows], 16-byte aligned
+  uint8_t* epi;                    // SB: [epilogue warp][slot][gate | up rows], 1024-byte aligned
 };
 
 template <class G>
@@ -93,7 +95,7 @@ __device__ __forceinline__ Smem carve(uint8_t* smem_raw) {
   s.abort_flag = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
   s.stage_info = reinterpret_cast<uint32_t*>(ctl + 512);
   s.rows = reinterpret_cast<uint32_t*>(ctl + 576);
-  s.epi = ctl + 576 + kProds * kRowMax * 4;
+  s.epi = ctl + G::EPI_OFF;
   return s;
 }
 
@@ -369,10 +371,16 @@ __device__ __forceinline__ void stage_gate_up(const Bf16Params& p, const Smem& s
   }
 }
 
-// SB: the linear's epilogue applies the SiLU*up backward (p.bwd_gate).
+// SB: the linear's epilogue applies the SiLU*up backward (p.bwd_gate).  At
+// B = 64 a lane's staged gate row and up row are 128 bytes with 16-byte chunk
+// c at c ^ (lane & 7) — the 128-byte-swizzled layout of a TMA box of 32 rows
+// x 64 columns — so d_gate / d_up are written over them in place and leave
+// as two TMA stores through `tm_out` ([T, 2 d_ff] bf16, 64 x 32 boxes).
 template <int B, bool GU, class G, bool SB = false>
-__device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int i_base, const Ctl& ctl) {
+__device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int i_base, const Ctl& ctl,
+                         const CUtensorMap* tm_out = nullptr) {
   static_assert(!(GU && SB), "the SiLU*up backward epilogue is a linear mode");
+  constexpr bool TSTORE = SB && B == 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
   const int nl = local_units(p.n_mtiles * p.R);
@@ -410,6 +418,10 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
           cp_async_commit();
         }
         if (i + 1 < nl) {
+          if constexpr (TSTORE) {  // slot (i+1)&1 is the source of unit i-1's stores
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
           int m2, r2;
           unit_mr(blockIdx.x + (i + 1) * gridDim.x, p, m2, r2);
           stage_gate_up<B, G>(p, s, m2, r2, q, lane, (i + 1) & 1);
@@ -425,6 +437,9 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
     // warp-uniform before the collective tcgen05.ld
     if (!__all_sync(0xffffffffu, mbar_wait(&s.acc_full[ab], use & 1u, ctl))) {
       if constexpr (SB) cp_async_wait_group<0>();  // no copy into shared memory outlives the CTA
+      if constexpr (TSTORE) {
+        if (lane == 0) bulk_wait_group0();
+      }
       return false;
     }
     tc_fence_after();
@@ -500,8 +515,14 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
               og[w] = pack_bf16x2(dg0, dg1);
               ou[w] = pack_bf16x2(du0, du1);
             }
-            st_global_v4(orow + t * 8, og[0], og[1], og[2], og[3]);
-            st_global_v4(orow + p.du_off + t * 8, ou[0], ou[1], ou[2], ou[3]);
+            if constexpr (TSTORE) {  // in place over the staged gate / up chunk
+              *reinterpret_cast<uint4*>(const_cast<uint8_t*>(gu_row) + c * 16) = make_uint4(og[0], og[1], og[2], og[3]);
+              *reinterpret_cast<uint4*>(const_cast<uint8_t*>(gu_row) + 32 * B * 2 + c * 16) =
+                  make_uint4(ou[0], ou[1], ou[2], ou[3]);
+            } else {
+              st_global_v4(orow + t * 8, og[0], og[1], og[2], og[3]);
+              st_global_v4(orow + p.du_off + t * 8, ou[0], ou[1], ou[2], ou[3]);
+            }
           }
         } else if (row_ok) {
           const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
@@ -538,6 +559,21 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.acc_empty[ab]);
+    if constexpr (TSTORE) {  // this warp's 32 rows of d_gate and d_up, out of the staging slot
+      const int64_t row0 = int64_t(m) * kBM + q * 32;
+      fence_proxy_async_smem();  // the in-place writes above -> visible to the TMA engine
+      __syncwarp();
+      if (lane == 0 && row0 < p.T) {  // rows past T are clipped by the map
+        const uint8_t* slot = s.epi + (q * G::EPI_NSLOT + (G::EPI_NSLOT == 2 ? (i & 1) : 0)) * G::EPI_SLOT;
+        tma_store_2d(tm_out, slot, int32_t(r) * B, int32_t(row0));
+        tma_store_2d(tm_out, slot + 32 * B * 2, int32_t(p.du_off + int64_t(r) * B), int32_t(row0));
+        bulk_commit_group();
+      }
+      __syncwarp();
+    }
+  }
+  if constexpr (TSTORE) {
+    if (lane == 0) bulk_wait_group0();
   }
   return true;
 }
