@@ -98,3 +98,19 @@ def test_ternary_config3_row_sample():
     np.testing.assert_array_equal(host(out[rows]), ref)
     from looped_blockell.kernels import read_status
     assert read_status() == 0
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_ternary_random_shapes_bit_exact(seed):
+    """Seeded random shapes, slot counts, dead slots and ragged token counts:
+    the gate / up pre-activations stay bit-exact."""
+    rng = np.random.default_rng(500 + seed)
+    Cd, Rf = int(rng.integers(2, 6)), int(rng.integers(2, 9))
+    T = int(rng.integers(1, 600))
+    Kg, Ku, Kd = int(rng.integers(1, Cd + 1)), int(rng.integers(1, Cd + 1)), int(rng.integers(1, Rf + 1))
+    case = make_case(T, Cd * 64, Rf * 64, 64, Kg, Ku, Kd, seed=seed, dead=int(rng.integers(0, 3)))
+    x, ws, out, m = _run(case, bool(seed % 2))
+    q_x, s_x = O.activation_quantize_int(x)
+    np.testing.assert_array_equal(ws["q_x"], q_x)
+    np.testing.assert_array_equal(ws["gate"], O.ternary_block_ell_matmul(q_x, s_x, *m["g"]))
+    np.testing.assert_array_equal(ws["up"], O.ternary_block_ell_matmul(q_x, s_x, *m["u"]))
