@@ -14,6 +14,10 @@
  * (BellFFNDesc.status, or the library's own word when NULL) and skip the work;
  * bell_read_status() returns and clears it.
  *
+ * T = 0 (no tokens) is a valid call: the weights and shapes are checked, the
+ * token-sized buffers (activations, outputs, h, plan) may be NULL, nothing is
+ * launched and the result is BELL_OK.
+ *
  * Block-ELL weight (looped_blockell/layers/block_ell.py:1-9,53-66 of the
  * reference): values [R, K, B, B] dense tiles and col_indices [R, K] int32.
  * The logical weight is [R*B, C*B]; y = x @ W^T.  Tile layout

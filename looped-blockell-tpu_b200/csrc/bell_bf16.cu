@@ -561,7 +561,8 @@ int check_ffn(const BellFFNDesc* d, int dtype) {
     return fail(BELL_ERR_SHAPE, "values_down R_model=" + std::to_string(w.R) + " inconsistent with d_model=" +
                                     std::to_string(d->d_model));
   if (int64_t(w.C) * w.B != d->d_ff) return fail(BELL_ERR_SHAPE, "down C*B inconsistent with d_ff");
-  if (!d->x || !d->h || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, h, out and plan must be non-NULL");
+  if (d->T > 0 && (!d->x || !d->h || !d->out || !d->plan))
+    return fail(BELL_ERR_ARG, "x, h, out and plan must be non-NULL");
   if (!aligned16(d->x) || !aligned16(d->h) || !aligned16(d->out) || !aligned16(d->plan))
     return fail(BELL_ERR_ALIGN, "x, h, out and plan must be 16-byte aligned");
   if ((d->gate_pre && !aligned16(d->gate_pre)) || (d->up_out && !aligned16(d->up_out)) ||
@@ -673,8 +674,8 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
     return fail(BELL_ERR_DTYPE, "bell_linear_bf16: out_dtype must be BELL_DTYPE_BF16 or BELL_DTYPE_F32");
   if (int rc = check_ell(d->w, "weight")) return rc;
   if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
-  if (!d->x || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, out and plan must be non-NULL");
-  if (d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
+  if (d->T > 0 && (!d->x || !d->out || !d->plan)) return fail(BELL_ERR_ARG, "x, out and plan must be non-NULL");
+  if (d->T > 0 && d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
   if (!aligned16(d->x) || !aligned16(d->out) || !aligned16(d->plan) || (d->residual && !aligned16(d->residual)))
     return fail(BELL_ERR_ALIGN, "x, out, residual and plan must be 16-byte aligned");
   if (int rc = require_sm100()) return rc;

@@ -173,8 +173,9 @@ int bell_swiglu_fwd_f32(const BellFFNDesc* d, void* stream) {
   if (int64_t(g.C) * g.B != d->d_model || int64_t(g.R) * g.B != d->d_ff || int64_t(w.R) * w.B != d->d_model ||
       int64_t(w.C) * w.B != d->d_ff)
     return fail(BELL_ERR_SHAPE, "gate/up/down shapes inconsistent with d_model / d_ff");
-  if (!d->x || !d->h || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, h, out and plan must be non-NULL");
   if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (d->T > 0 && (!d->x || !d->h || !d->out || !d->plan))
+    return fail(BELL_ERR_ARG, "x, h, out and plan must be non-NULL");
   if (int rc = require_sm100()) return rc;
   if (d->T == 0) return BELL_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -232,9 +233,9 @@ int bell_linear_f32(const BellLinearDesc* d, void* stream) {
   if (d->dtype != BELL_DTYPE_F32 || d->out_dtype != BELL_DTYPE_F32)
     return fail(BELL_ERR_DTYPE, "bell_linear_f32: dtype and out_dtype must be BELL_DTYPE_F32");
   if (int rc = check_ell_f32(d->w, "weight")) return rc;
-  if (!d->x || !d->out || !d->plan) return fail(BELL_ERR_ARG, "x, out and plan must be non-NULL");
-  if (d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
   if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (d->T > 0 && (!d->x || !d->out || !d->plan)) return fail(BELL_ERR_ARG, "x, out and plan must be non-NULL");
+  if (d->T > 0 && d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
   if (int rc = require_sm100()) return rc;
   if (d->T == 0) return BELL_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

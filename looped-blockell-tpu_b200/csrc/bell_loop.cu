@@ -160,8 +160,9 @@ extern "C" {
 
 int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gain, float eps, void* out,
                       void* stream) {
-  if (!x || !gain || !out) return fail(BELL_ERR_ARG, "bell_rmsnorm_bf16: NULL pointer");
-  if (T < 0 || d_model <= 0 || d_model % 8 != 0) return fail(BELL_ERR_SHAPE, "bell_rmsnorm_bf16: d_model % 8 != 0");
+  if (T < 0 || d_model <= 0 || d_model % 8 != 0)
+    return fail(BELL_ERR_SHAPE, "bell_rmsnorm_bf16: need T >= 0 and d_model a positive multiple of 8");
+  if (!gain || (T > 0 && (!x || !out))) return fail(BELL_ERR_ARG, "bell_rmsnorm_bf16: NULL pointer");
   if (!aligned16(x) || !aligned16(gain) || !aligned16(out)) return fail(BELL_ERR_ALIGN, "bell_rmsnorm_bf16: alignment");
   if (int rc = require_sm100()) return rc;
   return launch_rmsnorm(x, gain, out, T, d_model, eps, static_cast<cudaStream_t>(stream));
@@ -170,10 +171,10 @@ int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gai
 int bell_inject_rmsnorm_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,
                              const float* log_dt, const void* gain, float eps, void* h_out, void* normed,
                              void* stream) {
-  if (!h || !e || !log_A || !log_dt || !gain || !h_out || !normed)
-    return fail(BELL_ERR_ARG, "bell_inject_rmsnorm_bf16: NULL pointer");
   if (T < 0 || d_model <= 0 || d_model % 8 != 0)
-    return fail(BELL_ERR_SHAPE, "bell_inject_rmsnorm_bf16: d_model % 8 != 0");
+    return fail(BELL_ERR_SHAPE, "bell_inject_rmsnorm_bf16: need T >= 0 and d_model a positive multiple of 8");
+  if (!log_A || !log_dt || !gain || (T > 0 && (!h || !e || !h_out || !normed)))
+    return fail(BELL_ERR_ARG, "bell_inject_rmsnorm_bf16: NULL pointer");
   if (!aligned16(h) || !aligned16(e) || !aligned16(gain) || !aligned16(h_out) || !aligned16(normed))
     return fail(BELL_ERR_ALIGN, "bell_inject_rmsnorm_bf16: alignment");
   if (int rc = require_sm100()) return rc;
@@ -187,8 +188,8 @@ int bell_inject_rmsnorm_bf16(int64_t T, int32_t d_model, const void* h, const vo
 
 int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,
                              const float* log_dt, void* out, void* stream) {
-  if (!h || !e || !log_A || !log_dt || !out) return fail(BELL_ERR_ARG, "bell_diag_injection_bf16: NULL pointer");
   if (T < 0 || d_model <= 0) return fail(BELL_ERR_SHAPE, "bell_diag_injection_bf16: bad shape");
+  if (!log_A || !log_dt || (T > 0 && (!h || !e || !out))) return fail(BELL_ERR_ARG, "bell_diag_injection_bf16: NULL pointer");
   if (int rc = require_sm100()) return rc;
   const int64_t n = T * d_model;
   if (n == 0) return BELL_OK;
@@ -205,7 +206,7 @@ int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const vo
 int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
   if (d->L < 0) return fail(BELL_ERR_ARG, "L must be >= 0");
-  if (!d->h_in || !d->h_out || !d->norm_gain || !d->hn || !d->h_mid || !d->plan)
+  if (!d->norm_gain || (d->T > 0 && (!d->h_in || !d->h_out || !d->hn || !d->h_mid || !d->plan)))
     return fail(BELL_ERR_ARG, "h_in, h_out, norm_gain, hn, h_mid and plan must be non-NULL");
   BellFFNDesc f{};
   f.T = d->T;
@@ -226,7 +227,7 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   if (int rc = require_sm100()) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t bytes = size_t(d->T) * d->d_model * 2;
-  if (d->h_out != d->h_in) {
+  if (d->h_out != d->h_in && bytes > 0) {
     cudaError_t e = cudaMemcpyAsync(d->h_out, d->h_in, bytes, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("loop copy: ") + cudaGetErrorString(e));
   }

@@ -535,7 +535,7 @@ extern "C" int bell_swiglu_fwd_ternary(const BellTernaryFFNDesc* d, void* stream
       int64_t(w.C) * kB != d->d_ff)
     return fail(BELL_ERR_SHAPE, "gate/up/down shapes inconsistent with d_model / d_ff");
   if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
-  if (!d->x || !d->q_x || !d->s_x || !d->h || !d->q_h || !d->s_h || !d->out || !d->plan)
+  if (d->T > 0 && (!d->x || !d->q_x || !d->s_x || !d->h || !d->q_h || !d->s_h || !d->out || !d->plan))
     return fail(BELL_ERR_ARG, "x, q_x, s_x, h, q_h, s_h, out and plan must be non-NULL");
   if (!aligned16(d->x) || !aligned16(d->q_x) || !aligned16(d->q_h) || !aligned16(d->h) || !aligned16(d->out) ||
       (d->gate_pre && !aligned16(d->gate_pre)) || (d->up_out && !aligned16(d->up_out)))
