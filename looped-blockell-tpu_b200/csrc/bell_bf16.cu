@@ -419,7 +419,7 @@ int make_w_map(CUtensorMap* m, const BellEll& e) {
   return make_map_2d(m, e.values, MapType::BF16, e.B, rows, uint64_t(e.B) * 2, 64, 64, Swz::B128);
 }
 
-static int unit_band(bool gate_up, int R);
+static int unit_band(bool gate_up, const Bf16Params& p, int B);
 
 // B = 128 kernel family: 0 feature-major (default), 1 CTA-pair token-major,
 // 2 single-CTA token-major (BELL_BF16_KERNEL=fmajor|pair|single).
@@ -450,7 +450,7 @@ static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   if (int rc = device_sm_count(&sms)) return rc;
   Bf16Params p = p0;
   p.n_mtiles = int32_t((p.T + 255) / 256);
-  p.band = unit_band(GU, p.R);
+  p.band = unit_band(GU, p, 128);
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
   // persistent grid: as many CTA pairs as can be resident at once
@@ -473,15 +473,29 @@ static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   return check_launch(GU ? "bell gate/up pair kernel" : "bell linear pair kernel");
 }
 
-// Rows per band of the unit order: gate/up bands of 32 block-rows keep
-// 32 x (K_g + K_u) weight tiles hot in L2 while all token tiles pass; the down
-// projection's whole weight set is small enough to stay resident unbanded.
-static int unit_band(bool gate_up, int R) {
+// Rows per band of the unit order.  While the gate/up weight tiles of all
+// block-rows fit in kBandBudget bytes (about 3/4 of the 126 MB L2), the order
+// is unbanded: every token tile passes all block-rows, so its activation panel
+// is read from DRAM once and the weights stay L2-resident.  Larger weight sets
+// are cut into bands of that many bytes, each L2-resident while all token
+// tiles pass.  Unbanded measured faster than 32-row bands on every benchmark
+// shape (config 5, 67 MB of gate/up tiles: 26.0 against 27.5-28.0 ms, the
+// power-capped clock higher with the DRAM re-reads gone; config 2: 0.682
+// against 0.699 ms).  The down projection is unbanded.  BELL_BAND_ROWS
+// overrides the gate/up band.
+static constexpr int64_t kBandBudget = int64_t(96) << 20;
+static int unit_band(bool gate_up, const Bf16Params& p, int B) {
   static const int env = [] {
     const char* s = std::getenv("BELL_BAND_ROWS");
     return s ? std::atoi(s) : 0;
   }();
-  int band = gate_up ? (env > 0 ? env : 32) : R;
+  const int R = p.R;
+  int band = R;
+  if (gate_up) {
+    const int64_t row_bytes = int64_t(p.K0 + p.K1) * B * B * 2;
+    if (row_bytes > 0 && kBandBudget / row_bytes < R) band = int(kBandBudget / row_bytes);
+    if (env > 0) band = env;
+  }
   return band < 1 ? 1 : (band > R ? R : band);
 }
 
@@ -490,7 +504,7 @@ static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
                        cudaStream_t stream) {
   using G = eng::Geo<B, GU, SB>;
   Bf16Params p = p0;
-  p.band = unit_band(GU, p.R);
+  p.band = unit_band(GU, p, B);
   auto kern = bell_bf16_kernel<B, GU, W_MN, SB>;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), G::SMEM_BYTES)) return rc;
   int sms = 0;
@@ -509,7 +523,7 @@ static int dispatch_bf16(int B, int layout, const CUtensorMap& a, const CUtensor
   if (B == 64) return mn ? launch_bf16<64, GU, true>(a, w0, w1, p, s) : launch_bf16<64, GU, false>(a, w0, w1, p, s);
   if (b128_kernel() == 0) {
     Bf16Params q = p;
-    q.band = unit_band(GU, p.R);
+    q.band = unit_band(GU, p, 128);
     if (!GU && p.add_residual) {  // the feature-major linear reads the residual with TMA
       CUtensorMap mr;
       if (int rc = make_map_2d(&mr, p.residual, MapType::BF16, uint64_t(p.ld_out), uint64_t(p.T),
