@@ -106,6 +106,87 @@ class ShardedSwiGLU:
 
         return self.run_chunks(x, partial_fn, out, add_residual)
 
+    def forward_host(self, x_own: torch.Tensor, out_host: torch.Tensor = None, add_residual: bool = True,
+                     device=None) -> torch.Tensor:
+        """Host-buffer forward with token-sliced input and output.
+
+        ``x_own`` is this rank's token rows of x (``owned_rows`` order, bf16,
+        pinned host memory), ``[T / N, d_model]``; the result is the same rows of
+        the full forward, written to ``out_host`` (pinned, allocated when None).
+        Every rank needs all tokens for its d_ff shard, but only its own 1/N
+        crosses its host link: per chunk, the slice is copied in on a copy
+        stream, NCCL all-gathers the chunk over NVLink, the partial forward and
+        reduce-scatter run as in ``forward``, and a third stream adds the
+        residual to the chunk's reduced rows and copies them out once that
+        chunk's reduce-scatter is done, while later chunks compute.  The
+        all-gather of chunk i+1 is issued from the copy stream before chunk i
+        computes, so it overlaps that compute.  Returns after the copies out
+        have finished."""
+        import torch.distributed as dist
+        from .kernels.ops import block_ell_gate_up, block_ell_linear
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        T = x_own.shape[0] * self.world
+        n = pick_chunks(T, self.world, self.want_chunks)
+        Tc, per = T // n, T // n // self.world
+        d = self.d_model
+        if out_host is None:
+            out_host = torch.empty((T // self.world, d), dtype=torch.bfloat16).pin_memory()
+        xs = self._buf("xs", (T // self.world, d), torch.bfloat16, dev)
+        out = self._buf("out_own", (T // self.world, d), torch.bfloat16, dev)
+        xfull = [self._buf(f"xf{i}", (Tc, d), torch.bfloat16, dev) for i in range(2)]
+        partial = [self._buf(f"p{i}", (Tc, d), torch.bfloat16, dev) for i in range(2)]
+        h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, dev)
+        cur = torch.cuda.current_stream(dev)
+        s_in = self._stream("in", dev)
+        s_out = self._stream("out", dev)
+        s_in.wait_stream(cur)  # the buffers' previous users are done
+        s_out.wait_stream(cur)
+        done = [None] * n  # compute of chunk i finished with xfull[i % 2]
+
+        def gather(i):
+            # issued from s_in, so NCCL waits for the slice's copy in (and for the
+            # compute that last read xfull[i % 2]), not for the compute stream
+            with torch.cuda.stream(s_in):
+                xs[i * per:(i + 1) * per].copy_(x_own[i * per:(i + 1) * per], non_blocking=True)
+                if i >= 2:
+                    s_in.wait_event(done[i - 2])
+                return dist.all_gather_into_tensor(xfull[i % 2], xs[i * per:(i + 1) * per], group=self.group,
+                                                   async_op=True)
+
+        works = []
+        g_next = gather(0)
+        for i in range(n):
+            g_cur = g_next
+            if i + 1 < n:
+                g_next = gather(i + 1)  # overlaps this chunk's compute
+            g_cur.wait()
+            if i >= 2:
+                works[i - 2].wait()  # partial buffer i%2 is free again
+            block_ell_gate_up(xfull[i % 2], self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h)
+            block_ell_linear(h, self.vd, self.cd, out=partial[i % 2])
+            done[i] = torch.cuda.Event()
+            done[i].record(cur)
+            works.append(dist.reduce_scatter_tensor(out[i * per:(i + 1) * per], partial[i % 2],
+                                                    op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+            with torch.cuda.stream(s_out):
+                works[i].wait()  # s_out waits for this chunk's reduce-scatter
+                if add_residual:
+                    out[i * per:(i + 1) * per].add_(xs[i * per:(i + 1) * per])
+                out_host[i * per:(i + 1) * per].copy_(out[i * per:(i + 1) * per], non_blocking=True)
+        for w in works:
+            w.wait()
+        cur.wait_stream(s_out)
+        s_out.synchronize()
+        return out_host
+
+    def _stream(self, name, dev):
+        key = ("stream", name, dev.index)
+        st = self._bufs.get(key)
+        if st is None:
+            st = torch.cuda.Stream(device=dev)
+            self._bufs[key] = st
+        return st
+
     def run_chunks(self, x: torch.Tensor, partial_fn, out: torch.Tensor = None, add_residual: bool = True,
                    dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
         """The chunk pipeline of ``forward`` around any partial computation:

@@ -1,6 +1,7 @@
 """torchrun worker for tests/test_gpu_multi.py: the d_ff-sharded forward on N
 GPUs (NCCL reduce-scatter) against the single-GPU fused forward computed on
-each rank; every rank checks the token rows it owns.  Exit code 0 = pass."""
+each rank; every rank checks the token rows it owns, through the device-buffer
+forward and the token-sliced host-buffer forward.  Exit code 0 = pass."""
 
 import datetime
 import os
@@ -34,6 +35,15 @@ def main():
         err = float((out.float() - r).norm() / r.norm())
         print(f"rank {rank} {cfg.name}: rel-L2 vs single GPU {err:.3e}", flush=True)
         ok &= err < 1e-2
+        # host-buffer entry: this rank's token rows in, the same rows of the result out
+        x_own = c["x"].index_select(0, rows).cpu().pin_memory()
+        for _ in range(2):  # twice: the second call reuses the cached buffers and streams
+            out_h = model.forward_host(x_own)
+            same = torch.equal(out_h, out.cpu())
+            err_h = float((out_h.float() - r.cpu()).norm() / r.cpu().norm())
+            print(f"rank {rank} {cfg.name}: forward_host rel-L2 vs single GPU {err_h:.3e}, "
+                  f"bit-identical to forward: {same}", flush=True)
+            ok &= err_h < 1e-2
     t = torch.tensor([0 if ok else 1], device="cuda")
     dist.all_reduce(t)
     dist.barrier()
