@@ -79,6 +79,16 @@ class ShardedSwiGLU:
         self.want_chunks = chunks
         self._bufs = {}
 
+    def _chunking(self, T: int) -> Tuple[int, int, int]:
+        """(chunks, tokens per chunk, rows per rank per chunk) for T tokens.
+        Every rank must own the same number of rows of every chunk, so T has
+        to be a multiple of the world size; anything else would drop rows."""
+        n = pick_chunks(T, self.world, self.want_chunks)
+        if T % n or (T // n) % self.world:
+            raise ValueError(f"ShardedSwiGLU: T={T} tokens cannot be split evenly over {self.world} ranks; "
+                             f"pad the batch to a multiple of {self.world}")
+        return n, T // n, T // n // self.world
+
     def launches_per_step(self, T: int) -> int:
         # per chunk: plan + gate/up, plan + down (NCCL and the residual add are not counted)
         return 4 * pick_chunks(T, self.world, self.want_chunks)
@@ -97,7 +107,7 @@ class ShardedSwiGLU:
         """This rank's token slice of the full forward (bf16, CUDA)."""
         from .kernels.ops import block_ell_gate_up, block_ell_linear
         T = x.shape[0]
-        Tc = T // pick_chunks(T, self.world, self.want_chunks)
+        _, Tc, _ = self._chunking(T)
         h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, x.device)
 
         def partial_fn(xi: torch.Tensor, dst: torch.Tensor) -> None:
@@ -126,8 +136,7 @@ class ShardedSwiGLU:
         from .kernels.ops import block_ell_gate_up, block_ell_linear
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         T = x_own.shape[0] * self.world
-        n = pick_chunks(T, self.world, self.want_chunks)
-        Tc, per = T // n, T // n // self.world
+        n, Tc, per = self._chunking(T)
         d = self.d_model
         if out_host is None:
             out_host = torch.empty((T // self.world, d), dtype=torch.bfloat16).pin_memory()
@@ -196,9 +205,7 @@ class ShardedSwiGLU:
         added on the owned rows at the end."""
         import torch.distributed as dist
         T = x.shape[0]
-        n = pick_chunks(T, self.world, self.want_chunks)
-        Tc = T // n
-        per = Tc // self.world
+        n, Tc, per = self._chunking(T)
         if out is None:
             out = torch.empty((T // self.world, self.d_model), dtype=dtype, device=x.device)
         partial = [self._buf(f"p{i % 2}", (Tc, self.d_model), dtype, x.device) for i in range(n)]

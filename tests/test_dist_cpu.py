@@ -140,3 +140,21 @@ def test_gloo_chunked_reduce_scatter_reconstructs_output(world):
         p.join(timeout=60)
     assert all(n == 4 for _, n, _ in res), res
     assert all(err < 1e-12 for _, _, err in res), res
+
+
+@pytest.mark.parametrize("T", [10, 4097])
+def test_uneven_token_count_is_refused(T):
+    """A token count that does not split evenly over the ranks is refused
+    before any work (it would otherwise drop the leftover rows)."""
+    from looped_blockell.dist import ShardedSwiGLU
+    rng = np.random.default_rng(0)
+    R, C, K, B = 4, 2, 2, 64
+    v = torch.from_numpy(rng.standard_normal((R, K, B, B)).astype(np.float32)).to(torch.bfloat16)
+    cols = torch.tensor([[0, 1]] * R, dtype=torch.int32)
+    vd = torch.from_numpy(rng.standard_normal((C, K, B, B)).astype(np.float32)).to(torch.bfloat16)
+    cd = torch.tensor([[0, 3], [1, 2]], dtype=torch.int32)
+    model = ShardedSwiGLU(v, cols, v, cols, vd, cd, rank=0, world=4)
+    with pytest.raises(ValueError, match="cannot be split evenly"):
+        model.forward(torch.zeros((T, C * B), dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="cannot be split evenly"):
+        model._chunking(T)
