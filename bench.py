@@ -201,6 +201,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the parity check of the last step's output against the CPU oracle")
+    ap.add_argument("--check-rows", type=int, default=256, help="token rows per rank in the parity check")
     ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd", "convert"],
                     help="time the forward, the backward, or the dense -> Block-ELL conversion of the gate weight")
     args = ap.parse_args()
@@ -397,6 +400,28 @@ def run_convert(args, cfg, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def parity_check(cfg, c, lay, out, rows, n_rows: int, seed: int = 0):
+    """rel-L2 of ``out`` (this rank's result rows; ``rows`` = their token
+    indices) against the CPU oracle on a sample of ``n_rows`` of them,
+    computed from the same bf16 inputs the GPU saw.  Runs outside the timed
+    region."""
+    import numpy as np
+    import torch
+    import oracle as O
+    n = min(n_rows, out.shape[0])
+    pick = np.sort(np.random.default_rng(seed).choice(out.shape[0], n, replace=False))
+    tok = rows[torch.from_numpy(pick)].to(c["x"].device)
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    x = f(c["x"].index_select(0, tok))
+    w = [(f(c[v]), c[cc].cpu().numpy(), lay) for v, cc in (("vg", "cg"), ("vu", "cu"), ("vd", "cd"))]
+    if cfg.L > 1:
+        ref = O.looped_ffn(x, np.ones(cfg.d_model), *w, L=cfg.L)
+    else:
+        ref = O.swiglu_ffn(x, *w, add_residual=True)
+    got = f(out.index_select(0, torch.from_numpy(pick).to(out.device)))
+    return O.rel_l2(got, ref), n
+
+
 def _events(torch):
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
@@ -503,6 +528,26 @@ def run_gpu(args, cfg, rank, world):
     value = T / (ms / 1e3)
     tflops = cfg.nnz_flops() / (ms / 1e3) / 1e12
 
+    # parity of one more (untimed) step's output against the CPU oracle: every
+    # rank checks a sample of the token rows it holds; the worst rank is reported
+    parity = None
+    if not args.no_check and cfg.dtype == "bf16":
+        import torch as _t
+        res = step(x)
+        _t.cuda.synchronize()
+        if world > 1:
+            from looped_blockell.dist import owned_rows, pick_chunks
+            rows = owned_rows(T, rank, world, pick_chunks(T, world, model.want_chunks))
+        else:
+            rows = _t.arange(T)
+        err, n_chk = parity_check(cfg, c, lay, res, rows, args.check_rows, seed=rank)
+        if world > 1:
+            t = _t.tensor([err], device="cuda", dtype=_t.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            err = float(t.item())
+        parity = {"rel_l2": err, "tolerance": 1e-2, "rows_per_rank": n_chk, "ranks": world,
+                  "oracle": "oracle/bell_oracle.py (fp64, on the bf16 inputs)"}
+
     # dominant kernel: the fused gate/up kernel, timed alone with events
     gu = None
     if world == 1 and cfg.L == 1 and cfg.dtype == "bf16":
@@ -597,6 +642,7 @@ def run_gpu(args, cfg, rank, world):
             "hbm": hbm_line(cfg, T, ms, world, hbm_peak, peak_src),
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(), "e2e": e2e,
+            "parity_rel_l2": None if parity is None else parity["rel_l2"], "parity": parity,
         }
         if gu:
             traffic = GU_DRAM_BYTES.get((args.config, cfg.T))

@@ -132,8 +132,10 @@ int bell_swiglu_fwd_bf16(const BellFFNDesc* desc, void* stream);
  * reserved on every GPU that loads it); desc->h and desc->plan must be NULL.
  * Rejects problems needing more than that (see bell_noalloc_scratch_bytes)
  * with BELL_ERR_SHAPE.  The first call on a device looks up the array's
- * address; make it before any stream capture.  Calls share the array, so
- * calls that overlap on the GPU race.  Allocates nothing.
+ * address; make it before any stream capture.  That address is kept for the
+ * life of the process's primary context on the device: do not keep using the
+ * library across a cudaDeviceReset.  Calls share the array, so calls that
+ * overlap on the GPU race.  Allocates nothing.
  */
 #define BELL_NOALLOC_SCRATCH_BYTES (32u << 20)
 int bell_swiglu_fwd_bf16_noalloc(const BellFFNDesc* desc, void* stream);

@@ -1,5 +1,6 @@
 // bell_common.cu — host helpers (errors, device info, tensor maps, status
 // word, L2 persistence window) and the tile-schedule plan kernel.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -26,8 +27,9 @@ int ok() { return BELL_OK; }
 // ------------------------------------------------------------- device info
 
 static constexpr int kMaxDev = 64;
-static int g_sm_count[kMaxDev] = {0};
-static int g_cc_major[kMaxDev] = {0};
+// written once per device (benign repeats), read on every launch
+static std::atomic<int> g_sm_count[kMaxDev];
+static std::atomic<int> g_cc_major[kMaxDev];
 static std::mutex g_mu;
 
 static int cur_device(int* dev) {
@@ -46,9 +48,8 @@ int device_sm_count(int* sm_count) {
     cudaError_t e2 = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     if (e1 != cudaSuccess || e2 != cudaSuccess)
       return fail(BELL_ERR_LAUNCH, "cudaDeviceGetAttribute failed");
-    std::lock_guard<std::mutex> lk(g_mu);
-    g_cc_major[dev] = major;
-    g_sm_count[dev] = sms;
+    g_cc_major[dev].store(major);
+    g_sm_count[dev].store(sms);
   }
   *sm_count = g_sm_count[dev];
   return BELL_OK;
@@ -69,10 +70,15 @@ int require_sm100() {
 
 __device__ int32_t g_bell_status_word;
 
+// The address is cached per device ordinal for the life of the process's
+// primary context (the runtime API's context); a caller that resets the
+// device or binds another context to the ordinal must not reuse this library
+// across that change.
 int32_t* default_status_ptr() {
   int dev;
   if (cur_device(&dev)) return nullptr;
   static int32_t* ptrs[kMaxDev] = {nullptr};
+  std::lock_guard<std::mutex> lk(g_mu);
   if (ptrs[dev] == nullptr) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_bell_status_word);
@@ -80,7 +86,6 @@ int32_t* default_status_ptr() {
       fail(BELL_ERR_LAUNCH, std::string("cudaGetSymbolAddress(status): ") + cudaGetErrorString(e));
       return nullptr;
     }
-    std::lock_guard<std::mutex> lk(g_mu);
     ptrs[dev] = static_cast<int32_t*>(p);
   }
   return ptrs[dev];

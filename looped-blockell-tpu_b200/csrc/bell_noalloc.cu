@@ -16,7 +16,9 @@
 // process exits.  In host code the array's name is only a host-side stand-in,
 // never a device address, so its device address is looked up with
 // cudaGetSymbolAddress, once per device, on that device's first call (make
-// that first call before starting any stream capture).  All calls on a device
+// that first call before starting any stream capture).  The address stays
+// cached for the life of the process's primary context on that device, so
+// the library must not be used across a cudaDeviceReset.  All calls on a device
 // share the one array: calls that overlap on the GPU (on different streams,
 // without ordering between them) race on it.  The array keeps the last call's
 // contents; nothing needs clearing because each call writes every byte of the
@@ -61,9 +63,11 @@ static size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
 using namespace bell;
 
+// 0 for sizes no forward accepts (negative T or d_ff, or a block-row or slot
+// count below 1), so a caller can use it to ask whether a call fits.
 extern "C" size_t bell_noalloc_scratch_bytes(int64_t T, int32_t d_ff, int32_t R_gu, int32_t K_gate, int32_t K_up,
                                              int32_t R_down, int32_t K_down) {
-  if (T < 0 || d_ff < 0) return 0;
+  if (T < 0 || d_ff < 0 || R_gu < 1 || K_gate < 1 || K_up < 1 || R_down < 1 || K_down < 1) return 0;
   return up256(plan_layout(R_gu, K_gate, K_up, R_down, K_down).total) + up256(size_t(T) * size_t(d_ff) * 2);
 }
 
@@ -71,7 +75,13 @@ extern "C" int bell_swiglu_fwd_bf16_noalloc(const BellFFNDesc* desc, void* strea
   if (!desc) return fail(BELL_ERR_ARG, "descriptor is NULL");
   if (desc->h || desc->plan)
     return fail(BELL_ERR_ARG, "bell_swiglu_fwd_bf16_noalloc: h and plan must be NULL (they come from the static scratch)");
-  if (desc->T < 0 || desc->d_ff < 0) return fail(BELL_ERR_SHAPE, "T and d_ff must be >= 0");
+  {
+    // validate the whole descriptor first (stand-in h / plan addresses), so a
+    // wrong shape is reported as itself, not as a scratch-size problem
+    BellFFNDesc probe = *desc;
+    probe.h = probe.plan = reinterpret_cast<void*>(uintptr_t(256));
+    if (int rc = check_ffn(&probe, BELL_DTYPE_BF16)) return rc;
+  }
   const size_t plan_b = up256(plan_layout(desc->gate.R, desc->gate.K, desc->up.K, desc->down.R, desc->down.K).total);
   const size_t need = plan_b + up256(size_t(desc->T) * size_t(desc->d_ff) * 2);
   if (need > size_t(BELL_NOALLOC_SCRATCH_BYTES))

@@ -108,3 +108,16 @@ def test_dense_roundtrip_matches_oracle_convention():
     np.testing.assert_array_equal(e.col_indices.numpy(), c)
     np.testing.assert_array_equal(e.values.numpy(), v)
     np.testing.assert_array_equal(block_ell_to_dense(e).numpy(), O.block_ell_to_dense(v, c, 128, 256))
+
+
+def test_noalloc_scratch_bytes_sizes():
+    """bell_noalloc_scratch_bytes: plan + h rounded to 256 bytes each, and 0
+    for any size no forward accepts (so a caller can ask whether a call fits)."""
+    lib = _lib().load()
+    plan = lib.bell_plan_bytes(16, 2, 3, 4, 6)
+    up = lambda v: (v + 255) & ~255  # noqa: E731
+    assert lib.bell_noalloc_scratch_bytes(700, 2048, 16, 2, 3, 4, 6) == up(plan) + up(700 * 2048 * 2)
+    assert lib.bell_noalloc_scratch_bytes(-1, 2048, 16, 2, 3, 4, 6) == 0
+    assert lib.bell_noalloc_scratch_bytes(700, 2048, -16, 2, 3, 4, 6) == 0
+    assert lib.bell_noalloc_scratch_bytes(700, 2048, 16, 0, 3, 4, 6) == 0
+    assert lib.bell_noalloc_scratch_bytes(700, 2048, 16, 2, 3, 4, -6) == 0

@@ -124,3 +124,38 @@ def test_errors_match_reference_checks():
         K.block_ell_swiglu_fwd(c["x"], c["vg"], c["cg"].long(), c["vu"], c["cu"], c["vd"], c["cd"])
     with pytest.raises(RuntimeError, match="same R_ff"):
         K.block_ell_swiglu_fwd(c["x"], c["vg"], c["cg"], c["vu"][:4], c["cu"][:4], c["vd"], c["cd"])
+
+
+@pytest.mark.parametrize("shared,layout", [(False, O.LAYOUT_IN_OUT), (True, O.LAYOUT_IN_OUT),
+                                           (False, O.LAYOUT_OUT_IN)])
+def test_config5_full_size_row_sample(shared, layout):
+    """BASELINE config 5 (T=262144, d=4096, F=16384, B=128, 25 %), the
+    benchmark's exact call (bench.py: make_ffn, independent gate/up
+    topologies unless --shared-gate-up, [B_in, B_out] tiles unless --layout
+    out_in), at full size on one GPU.  This runs the feature-major B = 128
+    kernels through every path the benchmark takes: 1024 token tiles x 128
+    block-rows of persistent-unit wrap-around, K = 8 gate/up and K = 32 down
+    plan rows, 64-bit offsets into the 8.6 GB h.  The oracle checks a
+    1024-token sample (tokens are independent), spread over the whole token
+    range so early, late and wrapped-around units are all covered."""
+    from looped_blockell.synth import CONFIGS, make_ffn
+    K = _kernels()
+    cfg = CONFIGS[5]
+    c = make_ffn(cfg, device="cuda", shared_gate_up=shared)
+    ref_in = {k: (v.float().cpu().numpy().astype(np.float64) if k.startswith("v") else v.cpu().numpy())
+              for k, v in c.items() if k != "x"}
+    if layout == O.LAYOUT_OUT_IN:  # the same weights, stored [B_out, B_in]
+        for k in ("vg", "vu", "vd"):
+            c[k] = c[k].transpose(-1, -2).contiguous()
+    out = K.block_ell_swiglu_fwd(c["x"], c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], add_residual=True,
+                                 layout=layout, shared_topology=shared)
+    rows = np.sort(np.random.default_rng(5).choice(cfg.T, 1024, replace=False))
+    rows[0], rows[-1] = 0, cfg.T - 1
+    ridx = torch.from_numpy(rows).cuda()
+    ref_in["x"] = c["x"].index_select(0, ridx).float().cpu().numpy().astype(np.float64)
+    ro = oracle_ffn(ref_in, add_residual=True)[0]
+    got = out.index_select(0, ridx).float().cpu().numpy()
+    assert O.rel_l2(got, ro) < TOL_BF16
+    x0 = ref_in["x"]
+    assert O.rel_l2(got - x0, ro - x0) < 2e-2  # the FFN part alone, without the residual
+    assert K.read_status() == 0
