@@ -260,6 +260,12 @@ int bell_inject_rmsnorm_bf16(int64_t T, int32_t d_model, const void* h, const vo
 int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gain, float eps,
                       void* out, void* stream);
 
+/* RMSNorm in fp32 (fp32 x, gain and out; d_model % 4 == 0, pointers 16-byte
+ * aligned): the reference RMSNorm layer on fp32 activations
+ * (looped_blockell/layers/norms.py:8-15). */
+int bell_rmsnorm_f32(int64_t T, int32_t d_model, const float* x, const float* gain, float eps, float* out,
+                     void* stream);
+
 /* --------------------------------------------------------------- backward */
 
 /*
@@ -331,6 +337,11 @@ typedef struct BellSddmmDesc {
 } BellSddmmDesc;
 
 int bell_sddmm_bf16(const BellSddmmDesc* desc, void* stream);
+
+/* The same tile gradients for fp32 a and b (the fp32 training path; fp32
+ * accumulation on the CUDA cores, any tile size).  Rows lda / ldb elements
+ * apart (multiples of 4); grad_bf16 must be NULL. */
+int bell_sddmm_f32(const BellSddmmDesc* desc, void* stream);
 
 /* ------------------------------------------------------------- conversion */
 

@@ -402,7 +402,8 @@ struct EllArgs {
 static int check_ell(const BellEll& e, const char* name) {
   if (!e.values || !e.col_indices) return fail(BELL_ERR_ARG, std::string(name) + ": NULL values/col_indices");
   if (e.R < 1 || e.C < 1 || e.K < 1) return fail(BELL_ERR_SHAPE, std::string(name) + ": R, C, K must be >= 1");
-  if (e.B != 64 && e.B != 128) return fail(BELL_ERR_SHAPE, std::string(name) + ": tile size B must be 64 or 128");
+  if (e.B != 16 && e.B != 32 && e.B != 64 && e.B != 128)
+    return fail(BELL_ERR_SHAPE, std::string(name) + ": tile size B must be 16, 32, 64 or 128");
   if (e.K > 254) return fail(BELL_ERR_SHAPE, std::string(name) + ": K must be <= 254");
   if (e.C > 65535) return fail(BELL_ERR_SHAPE, std::string(name) + ": C must be <= 65535");
   if (e.layout != BELL_TILE_IN_OUT && e.layout != BELL_TILE_OUT_IN)
@@ -588,12 +589,19 @@ int check_ffn(const BellFFNDesc* d, int dtype) {
 
 int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   const BellEll &g = d->gate, &u = d->up;
+  const bool sm = g.B < 64;  // small tiles: bell_small.cu
   CUtensorMap ma, mg, mu;
-  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64, a_box_rows(g.B),
-                           Swz::B128))
-    return rc;
-  if (int rc = make_w_map(&mg, g)) return rc;
-  if (int rc = make_w_map(&mu, u)) return rc;
+  if (sm) {
+    if (int rc = make_small_x_map(&ma, d->x, d->d_model, d->T, g.B)) return rc;
+    if (int rc = make_small_w_map(&mg, g)) return rc;
+    if (int rc = make_small_w_map(&mu, u)) return rc;
+  } else {
+    if (int rc = make_map_2d(&ma, d->x, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64,
+                             a_box_rows(g.B), Swz::B128))
+      return rc;
+    if (int rc = make_w_map(&mg, g)) return rc;
+    if (int rc = make_w_map(&mu, u)) return rc;
+  }
   PlanLayout L = plan_layout(g.R, g.K, u.K, d->down.R, d->down.K);
   Bf16Params p{};
   p.T = d->T;
@@ -611,16 +619,23 @@ int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.status = status;
   p.timeout_ns = wait_budget_ns();
   p.split = use_split(d) ? 1 : 0;  // must match the plan built by launch_ffn_plan
+  if (sm) return launch_small(true, g.B, g.layout == BELL_TILE_IN_OUT, ma, mg, mu, p, s);
   return dispatch_bf16<true>(g.B, g.layout, ma, mg, mu, p, s);
 }
 
 int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   const BellEll& w = d->down;
+  const bool sm = w.B < 64;
   CUtensorMap ma, mw;
-  if (int rc = make_map_2d(&ma, d->h, MapType::BF16, d->d_ff, d->T, uint64_t(d->d_ff) * 2, 64, a_box_rows(w.B),
-                           Swz::B128))
-    return rc;
-  if (int rc = make_w_map(&mw, w)) return rc;
+  if (sm) {
+    if (int rc = make_small_x_map(&ma, d->h, d->d_ff, d->T, w.B)) return rc;
+    if (int rc = make_small_w_map(&mw, w)) return rc;
+  } else {
+    if (int rc = make_map_2d(&ma, d->h, MapType::BF16, d->d_ff, d->T, uint64_t(d->d_ff) * 2, 64, a_box_rows(w.B),
+                             Swz::B128))
+      return rc;
+    if (int rc = make_w_map(&mw, w)) return rc;
+  }
   PlanLayout L = plan_layout(d->gate.R, d->gate.K, d->up.K, w.R, w.K);
   Bf16Params p{};
   p.T = d->T;
@@ -638,6 +653,7 @@ int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.out_f32 = 0;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
+  if (sm) return launch_small(false, w.B, w.layout == BELL_TILE_IN_OUT, ma, mw, mw, p, s);
   return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
 }
 
@@ -700,10 +716,17 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   const BellEll& w = d->w;
   if (int rc = launch_plan(nullptr, 0, nullptr, 0, 0, 0, w.col_indices, w.K, w.R, w.C, d->plan, status, s)) return rc;
   const int64_t in_f = int64_t(w.C) * w.B, out_f = int64_t(w.R) * w.B;
+  const bool sm = w.B < 64;
   CUtensorMap ma, mw;
-  if (int rc = make_map_2d(&ma, d->x, MapType::BF16, in_f, d->T, uint64_t(in_f) * 2, 64, a_box_rows(w.B), Swz::B128))
-    return rc;
-  if (int rc = make_w_map(&mw, w)) return rc;
+  if (sm) {
+    if (int rc = make_small_x_map(&ma, d->x, in_f, d->T, w.B)) return rc;
+    if (int rc = make_small_w_map(&mw, w)) return rc;
+  } else {
+    if (int rc = make_map_2d(&ma, d->x, MapType::BF16, in_f, d->T, uint64_t(in_f) * 2, 64, a_box_rows(w.B),
+                             Swz::B128))
+      return rc;
+    if (int rc = make_w_map(&mw, w)) return rc;
+  }
   PlanLayout L = plan_layout(0, 0, 0, w.R, w.K);
   Bf16Params p{};
   p.T = d->T;
@@ -720,12 +743,16 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   p.out_f32 = d->out_dtype == BELL_DTYPE_F32 ? 1 : 0;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
+  if (sm) return launch_small(false, w.B, w.layout == BELL_TILE_IN_OUT, ma, mw, mw, p, s);
   return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
 }
 
 int bell_down_silu_bwd_bf16(const BellDownBwdDesc* d, void* stream) {
   if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
   if (int rc = check_ell(d->w_t, "w_t")) return rc;
+  if (d->w_t.B < 64)
+    return fail(BELL_ERR_SHAPE, "bell_down_silu_bwd_bf16: tile size must be 64 or 128 (use bell_linear_bf16 + "
+                                "bell_silu_mul_bwd_bf16 for smaller tiles)");
   if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
   if (d->T > 0 && (!d->grad_out || !d->gate_pre || !d->up_out || !d->d_gate_up || !d->plan))
     return fail(BELL_ERR_ARG, "grad_out, gate_pre, up_out, d_gate_up and plan must be non-NULL");

@@ -74,6 +74,16 @@ __device__ __forceinline__ void unit_mr(int u, const Bf16Params& p, int& m, int&
 // BELL_GU_SPLIT override for the feature-major gate/up kernel: -1 automatic,
 // 0 fused steps, 1 one weight tile per step (plan built without merging)
 int fmajor_split_env();
+
+// Small-tile kernels (B = 16, 32), bell_small.cu: activation map with B x 128
+// boxes, weight map with one tile per box (32- / 64-byte swizzle).
+int make_small_x_map(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int B);
+int make_small_w_map(CUtensorMap* m, const BellEll& e);
+// Tile gradients on the CUDA cores (bf16 at B = 16, 32; fp32 operands at any
+// B); grad already zeroed or accumulating.
+int launch_sddmm_ffma(const BellSddmmDesc* d, bool f32, int32_t* status, cudaStream_t s);
+int launch_small(bool gate_up, int B, bool w_mn, const CUtensorMap& x, const CUtensorMap& w0, const CUtensorMap& w1,
+                 const Bf16Params& p, cudaStream_t stream);
 int launch_fmajor(bool gate_up, bool w_mn, const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap& w1,
                   const Bf16Params& p, cudaStream_t stream);
 

@@ -524,7 +524,8 @@ int bell_sddmm_bf16(const BellSddmmDesc* d, void* stream) {
   if (!d) return fail(BELL_ERR_ARG, "bell_sddmm_bf16: NULL descriptor");
   if (!d->col_indices || !d->grad || (d->T > 0 && (!d->a || !d->b)))
     return fail(BELL_ERR_ARG, "bell_sddmm_bf16: NULL pointer");
-  if (d->B != 64 && d->B != 128) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: tile size must be 64 or 128");
+  if (d->B != 16 && d->B != 32 && d->B != 64 && d->B != 128)
+    return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: tile size must be 16, 32, 64 or 128");
   if (d->T < 0 || d->R <= 0 || d->C <= 0 || d->K <= 0)
     return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: need T >= 0 and R, C, K > 0");
   if (d->T > INT32_MAX - 64) return fail(BELL_ERR_SHAPE, "bell_sddmm_bf16: T too large");
@@ -546,7 +547,9 @@ int bell_sddmm_bf16(const BellSddmmDesc* d, void* stream) {
     if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   }
   if (d->T > 0) {
-    const int rc = d->B == 64 ? launch_sddmm<64>(d, status, s, sms) : launch_sddmm<128>(d, status, s, sms);
+    const int rc = d->B < 64     ? launch_sddmm_ffma(d, false, status, s)
+                   : d->B == 64 ? launch_sddmm<64>(d, status, s, sms)
+                                : launch_sddmm<128>(d, status, s, sms);
     if (rc) return rc;
   }
   if (d->grad_bf16) {
@@ -555,6 +558,33 @@ int bell_sddmm_bf16(const BellSddmmDesc* d, void* stream) {
     return check_launch("bell_f32_to_bf16_kernel");
   }
   return BELL_OK;
+}
+
+int bell_sddmm_f32(const BellSddmmDesc* d, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "bell_sddmm_f32: NULL descriptor");
+  if (!d->col_indices || !d->grad || (d->T > 0 && (!d->a || !d->b)))
+    return fail(BELL_ERR_ARG, "bell_sddmm_f32: NULL pointer");
+  if (d->grad_bf16) return fail(BELL_ERR_ARG, "bell_sddmm_f32: grad_bf16 must be NULL (the gradient is fp32)");
+  if (d->B != 16 && d->B != 32 && d->B != 64 && d->B != 128)
+    return fail(BELL_ERR_SHAPE, "bell_sddmm_f32: tile size must be 16, 32, 64 or 128");
+  if (d->T < 0 || d->R <= 0 || d->C <= 0 || d->K <= 0)
+    return fail(BELL_ERR_SHAPE, "bell_sddmm_f32: need T >= 0 and R, C, K > 0");
+  if (d->lda < int64_t(d->C) * d->B || d->ldb < int64_t(d->R) * d->B)
+    return fail(BELL_ERR_SHAPE, "bell_sddmm_f32: row pitch smaller than the row");
+  if (d->layout != BELL_TILE_IN_OUT && d->layout != BELL_TILE_OUT_IN)
+    return fail(BELL_ERR_ARG, "bell_sddmm_f32: unknown tile layout");
+  if (!aligned16(d->grad)) return fail(BELL_ERR_ALIGN, "bell_sddmm_f32: gradient buffer must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = d->status ? d->status : default_status_ptr();
+  if (!status) return BELL_ERR_LAUNCH;
+  if (!d->accumulate) {
+    const size_t n = size_t(d->R) * d->K * d->B * d->B;
+    cudaError_t e = cudaMemsetAsync(d->grad, 0, n * sizeof(float), s);
+    if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  }
+  if (d->T == 0) return BELL_OK;
+  return launch_sddmm_ffma(d, true, status, s);
 }
 
 }  // extern "C"

@@ -133,6 +133,7 @@ int make_map_2d(CUtensorMap* map, const void* base, MapType type, uint64_t inner
   cuuint32_t estr[2] = {1, 1};
   CUtensorMapSwizzle sw = swz == Swz::B128  ? CU_TENSOR_MAP_SWIZZLE_128B
                           : swz == Swz::B64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : swz == Swz::B32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                             : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                   l2_256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_L2_128B,

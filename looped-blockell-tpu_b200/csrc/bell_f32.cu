@@ -2,9 +2,9 @@
 //
 // tcgen05's fp32-input kind (tf32) keeps 10 mantissa bits and cannot meet a
 // 1e-5 relative-L2 target, so this path runs exact fp32 FFMA on CUDA cores:
-// a CTA computes a 64-token x 64-feature output tile, staging 32-wide K
-// chunks of the gathered activation tile and the weight tile(s) in shared
-// memory.  It shares the tile-schedule plan (bell_common.cu) with the bf16
+// a CTA computes a 64-token x min(B, 64)-feature output tile of one
+// block-row, staging min(B, 32)-wide K chunks of the gathered activation tile
+// and the weight tile(s) in shared memory (any tile size 16, 32, 64, 128).  It shares the tile-schedule plan (bell_common.cu) with the bf16
 // path, so dead slots, ragged K and gate/up column merging behave the same.
 // Semantics: looped_blockell/layers/block_ell.py:149-182 and mlp.py:119-145.
 #include <string>
@@ -15,8 +15,15 @@
 namespace bell {
 
 static constexpr int kTM = 64;   // tokens per CTA
-static constexpr int kTN = 64;   // output features per CTA
-static constexpr int kTK = 32;   // K chunk
+
+// Output tile = kTM tokens x TN features of one block-row (TN = min(B, 64)),
+// K chunks of TK = min(B, 32); 256 threads, each MI x 4 outputs.
+template <int TN>
+struct FTile {
+  static constexpr int TK = TN < 32 ? TN : 32;
+  static constexpr int TXN = TN / 4;        // threads along features
+  static constexpr int MI = kTM * TN / (256 * 4);  // token rows per thread
+};
 
 struct F32Params {
   int64_t T;
@@ -34,36 +41,39 @@ struct F32Params {
   int32_t add_residual;
 };
 
-__device__ __forceinline__ void load_w_f32(float (*ws)[kTN + 1], const float* w, int tile, int B, int layout, int kc,
+template <int TN, int TK>
+__device__ __forceinline__ void load_w_f32(float (*ws)[TN + 1], const float* w, int tile, int B, int layout, int kc,
                                            int n0) {
   const float* base = w + size_t(tile) * B * B;
   if (layout == BELL_TILE_IN_OUT) {
-    for (int idx = threadIdx.x; idx < kTK * kTN; idx += blockDim.x) {
-      const int i = idx / kTN, j = idx % kTN;
-      ws[i][j] = base[size_t(kc * kTK + i) * B + n0 + j];
+    for (int idx = threadIdx.x; idx < TK * TN; idx += blockDim.x) {
+      const int i = idx / TN, j = idx % TN;
+      ws[i][j] = base[size_t(kc * TK + i) * B + n0 + j];
     }
   } else {
-    for (int idx = threadIdx.x; idx < kTK * kTN; idx += blockDim.x) {
-      const int j = idx / kTK, i = idx % kTK;
-      ws[i][j] = base[size_t(n0 + j) * B + kc * kTK + i];
+    for (int idx = threadIdx.x; idx < TK * TN; idx += blockDim.x) {
+      const int j = idx / TK, i = idx % TK;
+      ws[i][j] = base[size_t(n0 + j) * B + kc * TK + i];
     }
   }
 }
 
-template <bool GU>
+template <bool GU, int TN>
 __global__ void __launch_bounds__(256) bell_f32_kernel(const F32Params p) {
-  __shared__ float xs[kTM][kTK + 1];
-  __shared__ float w0s[kTK][kTN + 1];
-  __shared__ float w1s[GU ? kTK : 1][kTN + 1];
+  using F = FTile<TN>;
+  constexpr int TK = F::TK, MI = F::MI;
+  __shared__ float xs[kTM][TK + 1];
+  __shared__ float w0s[TK][TN + 1];
+  __shared__ float w1s[GU ? TK : 1][TN + 1];
   const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
+  const int tx = tid % F::TXN, ty = tid / F::TXN;
   const int64_t units = int64_t(p.n_mtiles) * p.R * p.n_nchunks;
   for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
     const int nch = int(u % p.n_nchunks);
     const int r = int((u / p.n_nchunks) % p.R);
     const int64_t m = u / (int64_t(p.n_nchunks) * p.R);
-    const int n0 = nch * kTN;
-    float acc0[4][4] = {}, acc1[4][4] = {};
+    const int n0 = nch * TN;
+    float acc0[MI][4] = {}, acc1[MI][4] = {};
     const int cw = p.counts[r];
     const int n = cw & 0xFFFF;
     const uint32_t* plan = p.plan + size_t(r) * p.S;
@@ -72,25 +82,25 @@ __global__ void __launch_bounds__(256) bell_f32_kernel(const F32Params p) {
       const int c = int(e & 0xFFFFu);
       const uint32_t k0 = (e >> 16) & 0xFFu, k1 = e >> 24;
       const bool has0 = k0 != 255u, has1 = GU && k1 != 255u;
-      for (int kc = 0; kc < p.B / kTK; ++kc) {
-        for (int idx = tid; idx < kTM * kTK; idx += blockDim.x) {
-          const int i = idx / kTK, k = idx % kTK;
+      for (int kc = 0; kc < p.B / TK; ++kc) {
+        for (int idx = tid; idx < kTM * TK; idx += blockDim.x) {
+          const int i = idx / TK, k = idx % TK;
           const int64_t row = m * kTM + i;
-          xs[i][k] = row < p.T ? p.a[row * p.ld_a + int64_t(c) * p.B + kc * kTK + k] : 0.f;
+          xs[i][k] = row < p.T ? p.a[row * p.ld_a + int64_t(c) * p.B + kc * TK + k] : 0.f;
         }
-        if (has0) load_w_f32(w0s, p.w0, r * p.K0 + int(k0), p.B, p.layout, kc, n0);
-        if (GU && has1) load_w_f32(w1s, p.w1, r * p.K1 + int(k1), p.B, p.layout, kc, n0);
+        if (has0) load_w_f32<TN, TK>(w0s, p.w0, r * p.K0 + int(k0), p.B, p.layout, kc, n0);
+        if (GU && has1) load_w_f32<TN, TK>(w1s, p.w1, r * p.K1 + int(k1), p.B, p.layout, kc, n0);
         __syncthreads();
 #pragma unroll 4
-        for (int kk = 0; kk < kTK; ++kk) {
-          float a[4], b0[4];
+        for (int kk = 0; kk < TK; ++kk) {
+          float a[MI], b0[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) a[i] = xs[ty * 4 + i][kk];
+          for (int i = 0; i < MI; ++i) a[i] = xs[ty * MI + i][kk];
           if (has0) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) b0[j] = w0s[kk][tx * 4 + j];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < MI; ++i)
 #pragma unroll
               for (int j = 0; j < 4; ++j) acc0[i][j] = fmaf(a[i], b0[j], acc0[i][j]);
           }
@@ -100,7 +110,7 @@ __global__ void __launch_bounds__(256) bell_f32_kernel(const F32Params p) {
 #pragma unroll
               for (int j = 0; j < 4; ++j) b1[j] = w1s[kk][tx * 4 + j];
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
+              for (int i = 0; i < MI; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc1[i][j] = fmaf(a[i], b1[j], acc1[i][j]);
             }
@@ -111,8 +121,8 @@ __global__ void __launch_bounds__(256) bell_f32_kernel(const F32Params p) {
     }
     const bool any0 = (cw >> 16) & 1, any1 = (cw >> 17) & 1;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t row = m * kTM + ty * 4 + i;
+    for (int i = 0; i < MI; ++i) {
+      const int64_t row = m * kTM + ty * MI + i;
       if (row >= p.T) continue;
       const int64_t off = row * p.ld_out + int64_t(r) * p.B + n0 + tx * 4;
 #pragma unroll
@@ -134,20 +144,25 @@ __global__ void __launch_bounds__(256) bell_f32_kernel(const F32Params p) {
 }
 
 template <bool GU>
-static int launch_f32(const F32Params& p, cudaStream_t s) {
+static int launch_f32(F32Params p, cudaStream_t s) {
   int sms = 0;
   if (int rc = device_sm_count(&sms)) return rc;
+  const int tn = p.B < 64 ? p.B : 64;
+  p.n_nchunks = p.B / tn;
   const int64_t units = int64_t(p.n_mtiles) * p.R * p.n_nchunks;
   if (units == 0) return BELL_OK;
   const int64_t grid = units < int64_t(sms) * 8 ? units : int64_t(sms) * 8;
-  bell_f32_kernel<GU><<<int(grid), 256, 0, s>>>(p);
+  if (tn == 16) bell_f32_kernel<GU, 16><<<int(grid), 256, 0, s>>>(p);
+  else if (tn == 32) bell_f32_kernel<GU, 32><<<int(grid), 256, 0, s>>>(p);
+  else bell_f32_kernel<GU, 64><<<int(grid), 256, 0, s>>>(p);
   return check_launch(GU ? "bell f32 gate/up kernel" : "bell f32 linear kernel");
 }
 
 static int check_ell_f32(const BellEll& e, const char* name) {
   if (!e.values || !e.col_indices) return fail(BELL_ERR_ARG, std::string(name) + ": NULL values/col_indices");
   if (e.R < 1 || e.C < 1 || e.K < 1) return fail(BELL_ERR_SHAPE, std::string(name) + ": R, C, K must be >= 1");
-  if (e.B != 64 && e.B != 128) return fail(BELL_ERR_SHAPE, std::string(name) + ": tile size B must be 64 or 128");
+  if (e.B != 16 && e.B != 32 && e.B != 64 && e.B != 128)
+    return fail(BELL_ERR_SHAPE, std::string(name) + ": tile size B must be 16, 32, 64 or 128");
   if (e.K > 254 || e.C > 65535) return fail(BELL_ERR_SHAPE, std::string(name) + ": K <= 254 and C <= 65535");
   if (e.layout != BELL_TILE_IN_OUT && e.layout != BELL_TILE_OUT_IN)
     return fail(BELL_ERR_ARG, std::string(name) + ": unknown tile layout");
@@ -195,7 +210,6 @@ int bell_swiglu_fwd_f32(const BellFFNDesc* d, void* stream) {
   p.S = g.K + u.K;
   p.layout = g.layout;
   p.n_mtiles = int32_t((d->T + kTM - 1) / kTM);
-  p.n_nchunks = g.B / kTN;
   p.ld_a = d->d_model;
   p.ld_out = d->d_ff;
   p.a = static_cast<const float*>(d->x);
@@ -215,7 +229,6 @@ int bell_swiglu_fwd_f32(const BellFFNDesc* d, void* stream) {
   q.S = w.K;
   q.layout = w.layout;
   q.n_mtiles = p.n_mtiles;
-  q.n_nchunks = w.B / kTN;
   q.ld_a = d->d_ff;
   q.ld_out = d->d_model;
   q.a = static_cast<const float*>(d->h);
@@ -253,7 +266,6 @@ int bell_linear_f32(const BellLinearDesc* d, void* stream) {
   q.S = w.K;
   q.layout = w.layout;
   q.n_mtiles = int32_t((d->T + kTM - 1) / kTM);
-  q.n_nchunks = w.B / kTN;
   q.ld_a = int64_t(w.C) * w.B;
   q.ld_out = int64_t(w.R) * w.B;
   q.a = static_cast<const float*>(d->x);

@@ -28,7 +28,7 @@ int32_t* default_status_ptr();
 // Encode a 2-D tiled tensor map: `inner` contiguous elements per row,
 // `outer` rows, `pitch_bytes` between rows, box = box_inner x box_outer.
 enum class MapType { BF16, INT8, F32 };
-enum class Swz { NONE, B64, B128 };
+enum class Swz { NONE, B32, B64, B128 };
 int make_map_2d(CUtensorMap* map, const void* base, MapType type, uint64_t inner, uint64_t outer,
                 uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer, Swz swz, bool l2_256 = true);
 

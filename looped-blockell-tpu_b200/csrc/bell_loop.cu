@@ -53,6 +53,34 @@ __global__ void __launch_bounds__(256) bell_rmsnorm_kernel(const __nv_bfloat16* 
   }
 }
 
+// fp32 RMSNorm (fp32 in/out, fp32 gain), one warp per token row, the
+// reference layer's precision for fp32 activations (norms.py:8-15).
+__global__ void __launch_bounds__(256) bell_rmsnorm_f32_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ gain,
+                                                               float* __restrict__ out, int64_t T, int d, float eps) {
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const float* xr = x + row * d;
+  float* orow = out + row * d;
+  float ss = 0.f;
+  for (int i = lane * 4; i < d; i += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / float(d) + eps);
+  for (int i = lane * 4; i < d; i += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    const float4 g = *reinterpret_cast<const float4*>(gain + i);
+    *reinterpret_cast<float4*>(orow + i) = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+  }
+}
+
 // h = exp(-softplus(log_dt) * exp(log_A)) * h + softplus(log_dt) * e
 // (reference diagonal_injection_kernel, persistent_core.cu:53-83).
 __global__ void __launch_bounds__(256) bell_injection_kernel(const __nv_bfloat16* __restrict__ h,
@@ -166,6 +194,19 @@ int bell_rmsnorm_bf16(int64_t T, int32_t d_model, const void* x, const void* gai
   if (!aligned16(x) || !aligned16(gain) || !aligned16(out)) return fail(BELL_ERR_ALIGN, "bell_rmsnorm_bf16: alignment");
   if (int rc = require_sm100()) return rc;
   return launch_rmsnorm(x, gain, out, T, d_model, eps, static_cast<cudaStream_t>(stream));
+}
+
+int bell_rmsnorm_f32(int64_t T, int32_t d_model, const float* x, const float* gain, float eps, float* out,
+                     void* stream) {
+  if (T < 0 || d_model <= 0 || d_model % 4 != 0)
+    return fail(BELL_ERR_SHAPE, "bell_rmsnorm_f32: need T >= 0 and d_model a positive multiple of 4");
+  if (!gain || (T > 0 && (!x || !out))) return fail(BELL_ERR_ARG, "bell_rmsnorm_f32: NULL pointer");
+  if (!aligned16(x) || !aligned16(gain) || !aligned16(out)) return fail(BELL_ERR_ALIGN, "bell_rmsnorm_f32: alignment");
+  if (int rc = require_sm100()) return rc;
+  if (T == 0) return BELL_OK;
+  bell_rmsnorm_f32_kernel<<<unsigned((T + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, gain, out, T,
+                                                                                               d_model, eps);
+  return check_launch("bell_rmsnorm_f32_kernel");
 }
 
 int bell_inject_rmsnorm_bf16(int64_t T, int32_t d_model, const void* h, const void* e, const float* log_A,

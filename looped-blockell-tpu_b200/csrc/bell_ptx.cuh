@@ -370,6 +370,18 @@ __device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
+// Same for the 32-byte swizzle (CU_TENSOR_MAP_SWIZZLE_32B): 32-B rows, 8-row
+// atoms of 256 B.
+__device__ __forceinline__ uint64_t sdesc_sw32(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(6) << 61;  // SWIZZLE_32B
+  return d;
+}
+
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32, M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                                   // D: f32

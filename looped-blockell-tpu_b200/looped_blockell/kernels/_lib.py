@@ -107,10 +107,13 @@ SIGNATURES = {
                                            C.c_void_p, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p]),
     "bell_rmsnorm_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
                                     C.c_void_p]),
+    "bell_rmsnorm_f32": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
+                                   C.c_void_p]),
     "bell_silu_mul_bwd_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_int64, C.c_void_p]),
     "bell_down_silu_bwd_bf16": (C.c_int, [C.POINTER(BellDownBwdDesc), C.c_void_p]),
     "bell_sddmm_bf16": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
+    "bell_sddmm_f32": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
     "bell_dense_to_ell": (C.c_int, [C.POINTER(BellDenseToEllDesc), C.c_void_p]),
     "bell_pin_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "bell_unpin_l2": (C.c_int, [C.c_void_p]),

@@ -175,12 +175,17 @@ def block_ell_sddmm(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int
                     out_bf16: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Tile gradients ``grad[r, k] (+)= a[:, c*B:(c+1)*B]^T b[:, r*B:(r+1)*B]``
     (c = cols[r, k]) in fp32, in ``layout``.  ``a``: [T, C*B], ``b``: [T, R*B]
-    bf16; either may be a column slice of a wider row-major tensor.  When
-    ``out_bf16`` is given it receives a bf16 copy.  Returns ``grad``."""
+    bf16 (tcgen05 at B = 64, 128; CUDA cores at 16, 32) or fp32 (CUDA cores,
+    ``bell_sddmm_f32``); either may be a column slice of a wider row-major
+    tensor.  When ``out_bf16`` is given (bf16 operands only) it receives a
+    bf16 copy.  Returns ``grad``."""
     for name, t in (("a", a), ("b", b), ("col_indices", cols)):
         _check_cuda(name, t)
-    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
-        raise RuntimeError("a and b must be bf16")
+    f32 = a.dtype == torch.float32
+    if a.dtype != b.dtype or a.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("a and b must both be bf16 or both fp32")
+    if f32 and out_bf16 is not None:
+        raise RuntimeError("out_bf16 needs bf16 operands")
     if cols.dtype != torch.int32 or cols.dim() != 2:
         raise RuntimeError("col_indices must be int32 [R, K]")
     if a.dim() != 2 or b.dim() != 2 or a.shape[0] != b.shape[0]:
@@ -209,13 +214,15 @@ def block_ell_sddmm(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int
     d.grad = grad.data_ptr()
     d.grad_bf16 = out_bf16.data_ptr() if out_bf16 is not None else None
     d.status = None
+    fn = _lib.load().bell_sddmm_f32 if f32 else _lib.load().bell_sddmm_bf16
     with torch.cuda.device(a.device):
-        _lib.check(_lib.load().bell_sddmm_bf16(C.byref(d), _stream()), "block_ell_sddmm")
+        _lib.check(fn(C.byref(d), _stream()), "block_ell_sddmm")
     return grad
 
 
 def block_ell_swiglu_bwd(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, v_up, ci_up, v_down, ci_down,
-                         layout: int = TILE_IN_OUT, add_residual: bool = True, fuse_silu: Optional[bool] = None):
+                         layout: int = TILE_IN_OUT, add_residual: bool = True, fuse_silu: Optional[bool] = None,
+                         fp32_weight_grads: bool = False):
     """Returns ``(dx, d_v_gate, d_v_up, d_v_down)`` (bf16) like the reference
     titan::block_ell_swiglu_bwd (block_ell_ops.cpp:83-97).
 
@@ -227,7 +234,10 @@ def block_ell_swiglu_bwd(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, 
     ``fuse_silu`` (default: tile size 64 only) computes d_h in the down
     kernel's TMEM and applies the SiLU*up backward in its epilogue; at tile
     size 128 the separate feature-major d_h launch plus the elementwise pass
-    measured faster (config 5: 18.3 ms against 23.1 ms)."""
+    measured faster (config 5: 18.3 ms against 23.1 ms).
+
+    ``fp32_weight_grads`` returns the weight gradients as the fp32 sums
+    (for fp32 master weights) instead of their bf16 casts."""
     tensors = (("grad_out", grad_out), ("x", x), ("gate_pre_act", gate_pre_act), ("up_out", up_out), ("h", h),
                ("v_gate", v_gate), ("v_up", v_up), ("v_down", v_down))
     for name, t in tensors:
@@ -276,12 +286,19 @@ def block_ell_swiglu_bwd(grad_out, x, gate_pre_act, up_out, h, v_gate, ci_gate, 
     # 4. tile gradients, one fp32 buffer, one bf16 result buffer
     n_g, n_u, n_d = v_gate.numel(), v_up.numel(), v_down.numel()
     g32 = torch.empty(n_g + n_u + n_d, dtype=torch.float32, device=dev)
-    g16 = torch.empty(n_g + n_u + n_d, dtype=torch.bfloat16, device=dev)
-    d_vg, d_vu, d_vd = (g16[:n_g].view(v_gate.shape), g16[n_g:n_g + n_u].view(v_up.shape),
-                        g16[n_g + n_u:].view(v_down.shape))
-    block_ell_sddmm(x, dgu[:, :F], ci_gate, B, layout, grad=g32[:n_g].view(v_gate.shape), out_bf16=d_vg)
-    block_ell_sddmm(x, dgu[:, F:], ci_up, B, layout, grad=g32[n_g:n_g + n_u].view(v_up.shape), out_bf16=d_vu)
-    block_ell_sddmm(h, grad_out, ci_down, B, layout, grad=g32[n_g + n_u:].view(v_down.shape), out_bf16=d_vd)
+    f_vg, f_vu, f_vd = (g32[:n_g].view(v_gate.shape), g32[n_g:n_g + n_u].view(v_up.shape),
+                        g32[n_g + n_u:].view(v_down.shape))
+    if fp32_weight_grads:
+        d_vg = d_vu = d_vd = None
+    else:
+        g16 = torch.empty(n_g + n_u + n_d, dtype=torch.bfloat16, device=dev)
+        d_vg, d_vu, d_vd = (g16[:n_g].view(v_gate.shape), g16[n_g:n_g + n_u].view(v_up.shape),
+                            g16[n_g + n_u:].view(v_down.shape))
+    block_ell_sddmm(x, dgu[:, :F], ci_gate, B, layout, grad=f_vg, out_bf16=d_vg)
+    block_ell_sddmm(x, dgu[:, F:], ci_up, B, layout, grad=f_vu, out_bf16=d_vu)
+    block_ell_sddmm(h, grad_out, ci_down, B, layout, grad=f_vd, out_bf16=d_vd)
+    if fp32_weight_grads:
+        return dx, f_vg, f_vu, f_vd
     return dx, d_vg, d_vu, d_vd
 
 

@@ -202,16 +202,21 @@ def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, 
 
 
 def rmsnorm(x: torch.Tensor, gain: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
-    """bf16 RMSNorm ``x / sqrt(mean(x^2) + eps) * gain`` (looped_blockell/layers/norms.py:8-15)."""
+    """RMSNorm ``x / sqrt(mean(x^2) + eps) * gain`` (looped_blockell/layers/norms.py:8-15):
+    bf16 x and gain (fp32 math, bf16 out), or fp32 x and gain (fp32 throughout)."""
     _check_cuda("x", x)
-    if x.dtype != torch.bfloat16 or gain.dtype != torch.bfloat16:
-        raise RuntimeError("rmsnorm: x and gain must be bf16")
+    if x.dtype == torch.bfloat16 and gain.dtype == torch.bfloat16:
+        fn = _lib.load().bell_rmsnorm_bf16
+    elif x.dtype == torch.float32 and gain.dtype == torch.float32:
+        fn = _lib.load().bell_rmsnorm_f32
+    else:
+        raise RuntimeError("rmsnorm: x and gain must both be bf16 or both fp32")
     x = x.contiguous()
     out = torch.empty_like(x)
     d = x.shape[-1]
     with torch.cuda.device(x.device):
-        _lib.check(_lib.load().bell_rmsnorm_bf16(x.numel() // d, d, x.data_ptr(), gain.contiguous().data_ptr(),
-                                                 float(eps), out.data_ptr(), _stream()), "rmsnorm")
+        _lib.check(fn(x.numel() // d, d, x.data_ptr(), gain.contiguous().data_ptr(), float(eps), out.data_ptr(),
+                      _stream()), "rmsnorm")
     return out
 
 

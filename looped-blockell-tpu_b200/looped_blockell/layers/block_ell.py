@@ -126,14 +126,23 @@ def block_ell_to_dense(block_ell: BlockELLTensor) -> torch.Tensor:
 
 def block_ell_matmul(x: torch.Tensor, block_ell: BlockELLTensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``x [..., in_features] -> [..., out_features]`` on the sm_100a kernel
-    (reference block_ell.py:149-182: ``y = x @ W^T`` over the live tiles)."""
-    from ..kernels.ops import block_ell_linear
+    (reference block_ell.py:149-182: ``y = x @ W^T`` over the live tiles).
+
+    Differentiable in ``x``, ``block_ell.values`` and ``residual``, as the
+    reference's is (tests/test_block_ell.py:57-72): the backward runs the
+    transposed Block-ELL product and the tile-gradient kernel, and the values'
+    gradient comes back in their own dtype."""
     cfg = block_ell.config
     lead = x.shape[:-1]
     if x.shape[-1] != cfg.in_features:
         raise ValueError(f"x last dim {x.shape[-1]} != in_features {cfg.in_features}")
     x2 = x.reshape(-1, cfg.in_features)
-    res2 = None if residual is None else residual.reshape(-1, cfg.out_features)
-    v = block_ell.values.to(x.dtype)
-    y = block_ell_linear(x2, v, block_ell.col_indices.to(torch.int32), residual=res2)
+    res2 = None if residual is None else residual.reshape(-1, cfg.out_features).to(x.dtype)
+    cols = block_ell.col_indices.to(torch.int32)
+    if x.dtype == torch.bfloat16:
+        from ..kernels.autograd import block_ell_linear_ad
+        y = block_ell_linear_ad(x2.contiguous(), block_ell.values, cols, residual=res2)
+    else:
+        from ..kernels.autograd import block_ell_linear_f32_ad
+        y = block_ell_linear_f32_ad(x2.contiguous(), block_ell.values, cols, residual=res2)
     return y.reshape(*lead, cfg.out_features)

@@ -9,6 +9,15 @@ in the reference (mlp.py:84-95).  Dead tiles (alive_mask False) are passed to
 the kernel as column -1 and skipped, which equals zeroing them (mlp.py:73-77).
 The SwiGLU branch runs the fused sm_100a kernel; like the PyTorch mirror
 (interop/pt_model.py:862-867) its projections carry no bias.
+
+Both modules are trainable, as the reference's are: the forward and backward
+run on this package's kernels through the autograd nodes of
+``kernels.autograd`` (tile gradients summed in fp32).  The kernels read a
+bf16 copy of each ``values`` parameter; the copy (and the -1-masked column
+indices) is rebuilt only when the parameter or the topology buffers change,
+which in-place updates such as an optimizer step report through the tensor's
+version counter.  Writes through ``.data`` bypass that counter: call
+``refresh()`` after them.
 """
 
 from __future__ import annotations
@@ -51,21 +60,45 @@ class BlockELLLinear(nn.Module):
     def config(self) -> BlockELLConfig:
         return BlockELLConfig(R=self.R, C=self.C, K=self.K, B=self.tile_size)
 
+    def refresh(self) -> None:
+        """Drop the cached kernel copies (after writes through ``.data``)."""
+        self._kcache = {}
+
+    def _cached(self, name, key, make):
+        cache = self.__dict__.setdefault("_kcache", {})
+        hit = cache.get(name)
+        if hit is None or hit[0] != key:
+            hit = (key, make())
+            cache[name] = hit
+        return hit[1]
+
     def effective_col_indices(self) -> torch.Tensor:
         """col_indices with dead slots set to -1 (skipped by the kernel)."""
-        return torch.where(self.alive_mask, self.col_indices, torch.full_like(self.col_indices, -1)).to(torch.int32)
+        ci, am = self.col_indices, self.alive_mask
+        key = (ci.data_ptr(), ci._version, am.data_ptr(), am._version)
+        return self._cached("cols", key, lambda: torch.where(am, ci, torch.full_like(ci, -1)).to(torch.int32)
+                            .contiguous())
 
     def kernel_values(self) -> torch.Tensor:
-        return self.values.detach().to(self.dtype).contiguous()
+        """The tiles the kernels read (``values`` in the compute dtype)."""
+        v = self.values
+        if v.dtype == self.dtype and v.is_contiguous():
+            return v.detach()
+        key = (v.data_ptr(), v._version, v.dtype)
+        return self._cached("values", key, lambda: v.detach().to(self.dtype).contiguous())
 
     def as_block_ell(self) -> BlockELLTensor:
         return BlockELLTensor(values=self.kernel_values(), col_indices=self.effective_col_indices(), config=self.config)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        from ..kernels.ops import block_ell_linear
         lead = x.shape[:-1]
-        y = block_ell_linear(x.reshape(-1, self.in_features).to(self.dtype), self.kernel_values(),
-                             self.effective_col_indices())
+        x2 = x.reshape(-1, self.in_features).to(self.dtype)
+        if self.dtype == torch.bfloat16:
+            from ..kernels.autograd import block_ell_linear_ad
+            y = block_ell_linear_ad(x2, self.values, self.effective_col_indices(), compute=self.kernel_values())
+        else:  # fp32 accuracy path
+            from ..kernels.autograd import block_ell_linear_f32_ad
+            y = block_ell_linear_f32_ad(x2, self.values, self.effective_col_indices(), compute=self.kernel_values())
         if self.bias is not None:
             y = y + self.bias.to(y.dtype)
         return y.reshape(*lead, self.out_features)
@@ -97,13 +130,25 @@ class MLPBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, deterministic: bool = True, residual: bool = False) -> torch.Tensor:
         if self.use_swiglu:
-            from ..kernels.ops import block_ell_swiglu_fwd
             lead = x.shape[:-1]
             x2 = x.reshape(-1, self.d_model).to(self.dtype)
-            out = block_ell_swiglu_fwd(x2, self.w_gate.kernel_values(), self.w_gate.effective_col_indices(),
-                                       self.w_up.kernel_values(), self.w_up.effective_col_indices(),
-                                       self.w_down.kernel_values(), self.w_down.effective_col_indices(),
-                                       add_residual=residual, shared_topology=self.gate_up_shared)
+            g, u, d = self.w_gate, self.w_up, self.w_down
+            if self.dtype == torch.bfloat16:
+                from ..kernels.autograd import block_ell_swiglu_ad
+                out = block_ell_swiglu_ad(x2, g.values, g.kernel_values(), g.effective_col_indices(), u.values,
+                                          u.kernel_values(), u.effective_col_indices(), d.values, d.kernel_values(),
+                                          d.effective_col_indices(), add_residual=residual,
+                                          shared_topology=self.gate_up_shared)
+            elif torch.is_grad_enabled() and (x2.requires_grad or any(w.values.requires_grad for w in (g, u, d))):
+                # fp32 training: the three differentiable fp32 projections
+                # (the fused fp32 kernel has no backward of its own)
+                hh = F.silu(g(x2)) * u(x2)
+                out = d(hh) + (x2 if residual else 0)
+            else:  # fp32 inference: the fused fp32 kernel
+                from ..kernels.ops import block_ell_swiglu_fwd
+                out = block_ell_swiglu_fwd(x2.contiguous(), g.kernel_values(), g.effective_col_indices(),
+                                           u.kernel_values(), u.effective_col_indices(), d.kernel_values(),
+                                           d.effective_col_indices(), add_residual=residual)
             out = out.reshape(*lead, self.d_model)
         else:
             out = self.fc2(F.gelu(self.fc1(x)))

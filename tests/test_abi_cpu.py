@@ -56,7 +56,7 @@ def test_bad_shapes_rejected_before_any_launch():
     d = L.BellFFNDesc()
     d.T, d.d_model, d.d_ff, d.dtype = 16, 256, 512, L.BELL_DTYPE_BF16
     d.x = d.h = d.out = d.plan = 1024  # never dereferenced: validation fails first
-    d.gate = L.BellEll(1024, 1024, 8, 4, 2, 32, 0, 0)  # B = 32 unsupported
+    d.gate = L.BellEll(1024, 1024, 8, 4, 2, 48, 0, 0)  # B = 48 unsupported
     d.up = L.BellEll(1024, 1024, 8, 4, 2, 64, 0, 0)
     d.down = L.BellEll(1024, 1024, 4, 8, 2, 64, 0, 0)
     assert lib.bell_swiglu_fwd_bf16(C.byref(d), None) == -2
