@@ -204,6 +204,11 @@ def main():
     ap.add_argument("--no-check", action="store_true",
                     help="skip the parity check of the last step's output against the CPU oracle")
     ap.add_argument("--check-rows", type=int, default=256, help="token rows per rank in the parity check")
+    ap.add_argument("--sm-reserve", type=int, default=None,
+                    help="N>1: SMs kept out of the GEMM grids for NCCL (default BELL_SM_RESERVE or 16)")
+    ap.add_argument("--chunks", type=int, default=4, help="N>1: token chunks of the reduce-scatter pipeline")
+    ap.add_argument("--nccl-max-ctas", type=int, default=None,
+                    help="N>1: NCCL CTA cap (default: the SM reserve)")
     ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd", "convert"],
                     help="time the forward, the backward, or the dense -> Block-ELL conversion of the gate weight")
     args = ap.parse_args()
@@ -436,8 +441,13 @@ def run_gpu(args, cfg, rank, world):
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    sm_reserve = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        from looped_blockell.dist import default_sm_reserve, nccl_options
+        sm_reserve = default_sm_reserve() if args.sm_reserve is None else args.sm_reserve
+        nmax = args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local),
+                                pg_options=nccl_options(max_ctas=nmax or None))
     hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
     c = make_ffn(cfg, device="cuda", shared_gate_up=args.shared_gate_up)
     lay = ops.TILE_OUT_IN if args.layout == "out_in" else ops.TILE_IN_OUT
@@ -448,7 +458,8 @@ def run_gpu(args, cfg, rank, world):
     launches_per_step = 3
     if world > 1:
         from looped_blockell.dist import ShardedSwiGLU
-        model = ShardedSwiGLU(c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], rank, world)
+        model = ShardedSwiGLU(c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], rank, world, chunks=args.chunks,
+                              sm_reserve=sm_reserve)
         step_out = model.alloc_out(T, c["x"])
         launches_per_step = model.launches_per_step(T)
 
@@ -637,7 +648,10 @@ def run_gpu(args, cfg, rank, world):
             "config": {"workload": cfg.name, "T": T, "d_model": d, "d_ff": F, "B": cfg.B, "density": cfg.density,
                        "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
                        "parallelism": f"dff{world}" if world > 1 else "single",
-                       "L": cfg.L, "l2": l2_note},
+                       "L": cfg.L, "l2": l2_note,
+                       **({"chunks": args.chunks, "sm_reserve": sm_reserve,
+                           "nccl_max_ctas": args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve}
+                          if world > 1 else {})},
             "tflops_effective": tflops, "tflops_effective_per_gpu": tflops / world,
             "hbm": hbm_line(cfg, T, ms, world, hbm_peak, peak_src),
             "gpu_launches": launches_per_step * args.steps,

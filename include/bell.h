@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define BELL_ABI_VERSION 1
+#define BELL_ABI_VERSION 2
 
 enum {
   BELL_OK = 0,
@@ -97,6 +97,10 @@ typedef struct BellFFNDesc {
   void* plan;                  /* workspace                                  */
   BellEll gate, up, down;
   int32_t* status;             /* optional device status word (or NULL)      */
+  int32_t max_ctas;            /* cap on each persistent grid (0 = all SMs);
+                                  leaves SMs free for concurrent work such as a
+                                  collective on another stream               */
+  int32_t reserved;
 } BellFFNDesc;
 
 /* y = x @ W^T (+ residual): one Block-ELL linear. */
@@ -105,13 +109,17 @@ typedef struct BellLinearDesc {
   int32_t dtype;               /* element type of x and the weight tiles     */
   int32_t out_dtype;           /* element type of out (bf16 inputs: BF16/F32) */
   int32_t add_residual;
-  int32_t reserved;
+  int32_t max_ctas;            /* cap on the persistent grid (0 = all SMs)   */
   const void* x;               /* [T, C*B]                                   */
   const void* residual;        /* [T, R*B], element type = dtype              */
   void* out;                   /* [T, R*B]                                   */
   void* plan;                  /* workspace, bell_plan_bytes(0,0,0,R,K)      */
   BellEll w;
   int32_t* status;
+  /* bf16 only: with add_residual, the residual is added to output rows
+   * [residual_row_lo, residual_row_hi) only (both 0: every row).  At tile
+   * size 128 both bounds are multiples of 256 or equal to T. */
+  int64_t residual_row_lo, residual_row_hi;
 } BellLinearDesc;
 
 /* Workspace bytes for the tile-schedule plan of one forward. */
@@ -236,7 +244,16 @@ typedef struct BellLoopDesc {
   void* barrier;
   BellEll gate, up, down;
   int32_t* status;
+  int32_t mode;                /* BELL_LOOP_*                                 */
+  int32_t reserved;
 } BellLoopDesc;
+
+/* BellLoopDesc.mode: which implementation runs the L iterations. */
+enum {
+  BELL_LOOP_AUTO = 0,          /* the library's choice (the fastest it has)   */
+  BELL_LOOP_LAUNCHES = 1,      /* 1 + 3L stream-ordered kernel launches       */
+  BELL_LOOP_PERSISTENT = 2     /* one persistent kernel (tile size 64)        */
+};
 
 int bell_loop_fwd_bf16(const BellLoopDesc* desc, void* stream);
 

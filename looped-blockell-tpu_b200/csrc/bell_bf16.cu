@@ -344,7 +344,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int t = 0; t < 32; ++t) f[t] = any0 ? __uint_as_float(a[t]) : 0.f;
           if (row_ok) {
             const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
-            if (p.add_residual) {
+            if (p.add_residual && res_row(p, row)) {
               const __nv_bfloat16* rrow = static_cast<const __nv_bfloat16*>(p.residual) + off;
 #pragma unroll
               for (int t = 0; t < 4; ++t) {
@@ -469,7 +469,8 @@ static int launch_pair(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
     }
     mp = n < sms / 2 ? n : sms / 2;
   }
-  const int64_t pairs = units < mp ? units : mp;
+  int64_t pairs = units < mp ? units : mp;
+  if (p.max_ctas > 0 && pairs > p.max_ctas / 2) pairs = p.max_ctas / 2 > 0 ? p.max_ctas / 2 : 1;
   kern<<<int(2 * pairs), kThreads, C::SMEM, stream>>>(a, w0, w1, p);
   return check_launch(GU ? "bell gate/up pair kernel" : "bell linear pair kernel");
 }
@@ -512,8 +513,7 @@ static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   if (int rc = device_sm_count(&sms)) return rc;
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
-  const int grid = int(units < sms ? units : sms);
-  kern<<<grid, eng::kThreads, G::SMEM_BYTES, stream>>>(a, w0, w1, p);
+  kern<<<grid_size(units, sms, p.max_ctas), eng::kThreads, G::SMEM_BYTES, stream>>>(a, w0, w1, p);
   return check_launch(GU ? "bell gate/up kernel" : "bell linear kernel");
 }
 
@@ -584,6 +584,7 @@ int check_ffn(const BellFFNDesc* d, int dtype) {
       (d->residual && !aligned16(d->residual)))
     return fail(BELL_ERR_ALIGN, "optional buffers must be 16-byte aligned");
   if (d->T > (int64_t(1) << 31) - 256) return fail(BELL_ERR_SHAPE, "T too large");
+  if (d->max_ctas < 0) return fail(BELL_ERR_ARG, "max_ctas must be >= 0");
   return BELL_OK;
 }
 
@@ -619,6 +620,7 @@ int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.status = status;
   p.timeout_ns = wait_budget_ns();
   p.split = use_split(d) ? 1 : 0;  // must match the plan built by launch_ffn_plan
+  p.max_ctas = d->max_ctas;
   if (sm) return launch_small(true, g.B, g.layout == BELL_TILE_IN_OUT, ma, mg, mu, p, s);
   return dispatch_bf16<true>(g.B, g.layout, ma, mg, mu, p, s);
 }
@@ -651,6 +653,7 @@ int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.residual = d->residual ? d->residual : d->x;
   p.add_residual = d->add_residual ? 1 : 0;
   p.out_f32 = 0;
+  p.max_ctas = d->max_ctas;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
   if (sm) return launch_small(false, w.B, w.layout == BELL_TILE_IN_OUT, ma, mw, mw, p, s);
@@ -708,6 +711,12 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   if (d->T > 0 && d->add_residual && !d->residual) return fail(BELL_ERR_ARG, "add_residual needs a residual pointer");
   if (!aligned16(d->x) || !aligned16(d->out) || !aligned16(d->plan) || (d->residual && !aligned16(d->residual)))
     return fail(BELL_ERR_ALIGN, "x, out, residual and plan must be 16-byte aligned");
+  const bool res_all = d->residual_row_lo == 0 && d->residual_row_hi == 0;
+  if (!res_all && (d->residual_row_lo < 0 || d->residual_row_hi < d->residual_row_lo || d->residual_row_hi > d->T))
+    return fail(BELL_ERR_SHAPE, "residual rows must satisfy 0 <= lo <= hi <= T");
+  if (!res_all && d->w.B == 128 && ((d->residual_row_lo % 256) || (d->residual_row_hi % 256 && d->residual_row_hi != d->T)))
+    return fail(BELL_ERR_SHAPE, "at tile size 128 the residual rows must start and end on 256-row boundaries (or T)");
+  if (d->max_ctas < 0) return fail(BELL_ERR_ARG, "max_ctas must be >= 0");
   if (int rc = require_sm100()) return rc;
   if (d->T == 0) return BELL_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -743,6 +752,11 @@ int bell_linear_bf16(const BellLinearDesc* d, void* stream) {
   p.out_f32 = d->out_dtype == BELL_DTYPE_F32 ? 1 : 0;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
+  p.max_ctas = d->max_ctas;
+  if (!res_all) {  // hi >= 1 here; [k, k) adds the residual to no row
+    p.res_lo = d->residual_row_lo;
+    p.res_hi = d->residual_row_hi;
+  }
   if (sm) return launch_small(false, w.B, w.layout == BELL_TILE_IN_OUT, ma, mw, mw, p, s);
   return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
 }

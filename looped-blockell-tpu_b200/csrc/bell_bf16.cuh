@@ -42,7 +42,21 @@ struct Bf16Params {
   int64_t du_off;
   int32_t* status;
   uint64_t timeout_ns;
+  int32_t max_ctas;  // cap on the persistent grid (0 = all SMs)
+  int64_t res_lo, res_hi;  // linear: residual added to token rows [res_lo, res_hi) only
 };
+
+// Whether token row `row` gets the residual: res_hi == 0 means every row.
+__device__ __forceinline__ bool res_row(const Bf16Params& p, int64_t row) {
+  return p.res_hi == 0 || (row >= p.res_lo && row < p.res_hi);
+}
+
+// Persistent grid size: min(units, SMs, max_ctas when set).
+inline int grid_size(int64_t units, int sms, int32_t max_ctas) {
+  int64_t g = units < sms ? units : sms;
+  if (max_ctas > 0 && g > max_ctas) g = max_ctas;
+  return int(g < 1 ? 1 : g);
+}
 
 // d_gate, d_up of h = silu(g) * u for an incoming d_h (the reference
 // swiglu_bwd.cu:305-334 formula), fp32.  sigmoid(g) = 0.5 + 0.5 tanh(g / 2)

@@ -72,6 +72,14 @@ __device__ __forceinline__ void st_global_b16(void* p, uint16_t v) {
   asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(v) : "memory");
 }
 
+// Whether 256-token tile m gets the residual: the tile lies inside the
+// residual row range (the host keeps the range on 256-row boundaries or T).
+__device__ __forceinline__ bool unit_res(const Bf16Params& p, int m) {
+  if (p.res_hi == 0) return true;
+  const int64_t t0 = int64_t(m) * TN, t1 = t0 + TN < p.T ? t0 + TN : p.T;
+  return t0 >= p.res_lo && t1 <= p.res_hi;
+}
+
 template <bool GU, bool W_MN, bool SPLIT>
 __global__ void __launch_bounds__(kThr, 1)
     bell_bf16_fmajor_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w0,
@@ -140,7 +148,8 @@ __global__ void __launch_bounds__(kThr, 1)
         unit_mr(u, p, m, r);
         const int n = p.counts[r] & 0xFFFF;
         const uint32_t* plan = p.plan + size_t(r) * p.S;
-        const int n_uses = n * (B / kBK) + (res_mma ? B / kBK : 0);
+        const bool ures = res_mma && unit_res(p, m);
+        const int n_uses = n * (B / kBK) + (ures ? B / kBK : 0);
         for (int j = 0; j < n_uses && alive; ++j, ++g) {
           if (int(g & 1u) == pid) {
             if (!mbar_wait(&empty[stage], phase ^ 1, ctl)) {
@@ -215,8 +224,9 @@ __global__ void __launch_bounds__(kThr, 1)
       uint32_t phase = 0;
       bool alive = true, issued_any = false;
       for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x, ++i) {
-        int m_unused, r;
-        unit_mr(u, p, m_unused, r);
+        int m, r;
+        unit_mr(u, p, m, r);
+        const bool ures = res_mma && unit_res(p, m);
         const int buf = C::NBUF == 2 ? (i & 1) : 0;
         const uint32_t use = C::NBUF == 2 ? uint32_t(i >> 1) : uint32_t(i);
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, ctl)) break;
@@ -258,7 +268,7 @@ __global__ void __launch_bounds__(kThr, 1)
             }
           }
         }
-        for (int kc = 0; res_mma && alive && kc < B / kBK; ++kc) {  // acc += I x residual
+        for (int kc = 0; ures && alive && kc < B / kBK; ++kc) {  // acc += I x residual
           if (!mbar_wait(&full[stage], phase, ctl)) {
             alive = false;
             break;
@@ -300,7 +310,7 @@ __global__ void __launch_bounds__(kThr, 1)
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       const int cw = p.counts[r];
-      const bool any0 = ((cw >> 16) & 1) || res_mma, any1 = (cw >> 17) & 1;
+      const bool any0 = ((cw >> 16) & 1) || (res_mma && unit_res(p, m)), any1 = (cw >> 17) & 1;
       const int64_t feat = int64_t(r) * B + q * 32 + lane;
       const int64_t tok0 = int64_t(m) * TN + half * 128;
       const uint32_t lane_base = uint32_t(q * 32) << 16;
@@ -383,7 +393,7 @@ static int launch(const CUtensorMap& a, const CUtensorMap& w0, const CUtensorMap
   p.n_mtiles = int32_t((p.T + TN - 1) / TN);
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
-  kern<<<int(units < sms ? units : sms), kThr, C::SMEM, stream>>>(a, w0, w1, p);
+  kern<<<grid_size(units, sms, p.max_ctas), kThr, C::SMEM, stream>>>(a, w0, w1, p);
   return check_launch(GU ? "bell gate/up feature-major kernel" : "bell linear feature-major kernel");
 }
 

@@ -526,7 +526,7 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
           }
         } else if (row_ok) {
           const int64_t off = row * p.ld_out + int64_t(r) * B + j * 32;
-          if (p.add_residual) {
+          if (p.add_residual && res_row(p, row)) {
             const __nv_bfloat16* rrow = static_cast<const __nv_bfloat16*>(p.residual) + off;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {

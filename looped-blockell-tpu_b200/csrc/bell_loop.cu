@@ -165,19 +165,11 @@ int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d,
   return check_launch("bell_rmsnorm_kernel");
 }
 
-// The loop runs as one launch per phase (RMSNorm, gate/up, down) by default.
-// BELL_LOOP_KERNEL=persistent selects the single cooperative kernel
-// (bell_loop_kernel.cu; tile size 64, needs the barrier workspace).  It gives
-// the same results but is slower on B200 (config 4: 1.36 ms against 0.86 ms):
-// its 3 L grid barriers drain and refill the pipelines as the launch
-// boundaries do, and its down phase runs on the shallower gate/up ring.
+// The loop runs as one launch per phase (RMSNorm, gate/up, down) unless the
+// descriptor asks for the single persistent kernel (bell_loop_kernel.cu; tile
+// size 64, needs the barrier workspace).
 static bool use_persistent_loop(const BellLoopDesc* d) {
-  static const bool persistent = [] {
-    const char* e = std::getenv("BELL_LOOP_KERNEL");
-    return e && std::string(e) == "persistent";
-  }();
-  return persistent && d->gate.B == 64 && d->barrier && aligned16(d->barrier) && aligned16(d->norm_gain) &&
-         d->d_model % 8 == 0;
+  return d->mode == BELL_LOOP_PERSISTENT;
 }
 
 }  // namespace bell
@@ -249,6 +241,12 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   if (d->L < 0) return fail(BELL_ERR_ARG, "L must be >= 0");
   if (!d->norm_gain || (d->T > 0 && (!d->h_in || !d->h_out || !d->hn || !d->h_mid || !d->plan)))
     return fail(BELL_ERR_ARG, "h_in, h_out, norm_gain, hn, h_mid and plan must be non-NULL");
+  if (d->mode != BELL_LOOP_AUTO && d->mode != BELL_LOOP_LAUNCHES && d->mode != BELL_LOOP_PERSISTENT)
+    return fail(BELL_ERR_ARG, "unknown loop mode");
+  if (d->mode == BELL_LOOP_PERSISTENT &&
+      (d->gate.B != 64 || !d->barrier || !aligned16(d->barrier) || !aligned16(d->norm_gain) || d->d_model % 8 != 0))
+    return fail(BELL_ERR_SHAPE, "the persistent loop kernel needs tile size 64, d_model % 8 == 0 and an aligned "
+                                "barrier workspace");
   BellFFNDesc f{};
   f.T = d->T;
   f.d_model = d->d_model;
@@ -276,10 +274,7 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   int32_t* status = d->status ? d->status : default_status_ptr();
   if (!status) return BELL_ERR_LAUNCH;
   if (int rc = launch_ffn_plan(&f, status, s)) return rc;
-  if (use_persistent_loop(d)) {
-    const int rc = loop_persistent_bf16(d, status, s);
-    if (rc != BELL_ERR_LAUNCH) return rc;  // no cooperative grid: run the multi-launch loop
-  }
+  if (use_persistent_loop(d)) return loop_persistent_bf16(d, status, s);
   for (int it = 0; it < d->L; ++it) {
     if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
     if (int rc = gate_up_bf16(&f, status, s)) return rc;

@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(kThr, 1)
             for (int v = 0; v < 4; ++v) {
               if (r0 + (cc * 32 + v * 8) / B >= p.R) continue;
               float* fv = f + v * 8;
-              if (p.add_residual) {
+              if (p.add_residual && res_row(p, row)) {
                 const uint4 rv = ld_global_v4(static_cast<const __nv_bfloat16*>(p.residual) + off + v * 8);
                 const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
@@ -448,7 +448,7 @@ static int launch_t(const CUtensorMap& x, const CUtensorMap& w0, const CUtensorM
   const int64_t units = int64_t(p.n_mtiles) * ((p.R + C::G - 1) / C::G);
   if (units == 0) return BELL_OK;
   if (units > int64_t(INT32_MAX)) return fail(BELL_ERR_SHAPE, "too many work units");
-  kern<<<int(units < sms ? units : sms), kThr, C::SMEM, stream>>>(x, w0, w1, p);
+  kern<<<grid_size(units, sms, p.max_ctas), kThr, C::SMEM, stream>>>(x, w0, w1, p);
   return check_launch(GU ? "bell gate/up small-tile kernel" : "bell linear small-tile kernel");
 }
 

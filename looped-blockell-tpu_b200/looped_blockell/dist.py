@@ -11,13 +11,26 @@ the full output, and the residual is added on that slice only.
 The token axis is cut into ``chunks``; rank g receives, for every chunk, the
 g-th 1/N of that chunk's rows (``owned_rows``).  The reduce-scatter of chunk
 i runs on NCCL's stream while the kernels of chunk i+1 run, so the transfer
-overlaps compute.  The reference has no multi-GPU code; this follows the
-partitioning its scaling plan asks for.
+overlaps compute.  Two things make that overlap real on a B200:
+
+* the persistent GEMM grids hold every SM they are given for the whole
+  kernel, so a collective queued behind them waits for the next kernel
+  boundary.  ``sm_reserve`` SMs are kept out of the GEMM grids (their
+  ``max_ctas``), and ``nccl_options`` caps NCCL to that many CTAs on a
+  high-priority stream, so the reduce-scatter runs beside the next chunk's
+  kernels;
+* the residual is added in the down kernel's epilogue, by the owning rank
+  only (``residual_rows`` = its rows of the chunk), so the reduce-scatter
+  delivers finished rows and no pass over them follows.
+
+The reference has no multi-GPU code; this follows the partitioning its
+scaling plan asks for.
 """
 
 from __future__ import annotations
 
-from typing import List, Tuple
+import os
+from typing import List, Optional, Tuple
 
 import torch
 
@@ -57,6 +70,24 @@ def owned_rows(T: int, rank: int, world: int, chunks: int) -> torch.Tensor:
     return torch.cat(idx)
 
 
+def nccl_options(max_ctas: Optional[int] = None, high_priority: bool = True):
+    """Process-group options for ``init_process_group("nccl", pg_options=...)``
+    that let the reduce-scatter run beside the GEMM kernels: NCCL on a
+    high-priority stream, and at most ``max_ctas`` CTAs per collective (the SMs
+    the sharded forward leaves free; None keeps NCCL's own choice)."""
+    import torch.distributed as dist
+    opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=high_priority)
+    if max_ctas:
+        opts.config.max_ctas = int(max_ctas)
+        opts.config.min_ctas = min(int(max_ctas), 4)
+    return opts
+
+
+def default_sm_reserve() -> int:
+    """SMs kept out of the GEMM grids while collectives run (BELL_SM_RESERVE)."""
+    return int(os.environ.get("BELL_SM_RESERVE", "16"))
+
+
 def pick_chunks(T: int, world: int, want: int = 4) -> int:
     c = want
     while c > 1 and (T % c or (T // c) % world or (T // c // world) % 128):
@@ -67,7 +98,8 @@ def pick_chunks(T: int, world: int, want: int = 4) -> int:
 class ShardedSwiGLU:
     """This rank's share of a d_ff-split SwiGLU forward (bf16)."""
 
-    def __init__(self, vg, cg, vu, cu, vd, cd, rank: int, world: int, chunks: int = 4, group=None):
+    def __init__(self, vg, cg, vu, cu, vd, cd, rank: int, world: int, chunks: int = 4, group=None,
+                 sm_reserve: Optional[int] = None):
         R_f = vg.shape[0]
         self.B = vg.shape[2]
         self.rank, self.world, self.group = rank, world, group
@@ -77,7 +109,15 @@ class ShardedSwiGLU:
         self.vd, self.cd = repack_down(vd, cd, self.lo, self.hi)
         self.d_model = vd.shape[0] * self.B
         self.want_chunks = chunks
+        self.sm_reserve = default_sm_reserve() if sm_reserve is None else int(sm_reserve)
         self._bufs = {}
+
+    def grid_cap(self, dev) -> int:
+        """``max_ctas`` of this rank's GEMM launches (0 = every SM)."""
+        if self.world == 1 or self.sm_reserve <= 0:
+            return 0
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        return max(1, sms - self.sm_reserve)
 
     def _chunking(self, T: int) -> Tuple[int, int, int]:
         """(chunks, tokens per chunk, rows per rank per chunk) for T tokens.
@@ -90,7 +130,7 @@ class ShardedSwiGLU:
         return n, T // n, T // n // self.world
 
     def launches_per_step(self, T: int) -> int:
-        # per chunk: plan + gate/up, plan + down (NCCL and the residual add are not counted)
+        # per chunk: plan + gate/up, plan + down (the NCCL reduce-scatter is not counted)
         return 4 * pick_chunks(T, self.world, self.want_chunks)
 
     def alloc_out(self, T: int, x: torch.Tensor) -> torch.Tensor:
@@ -107,14 +147,25 @@ class ShardedSwiGLU:
         """This rank's token slice of the full forward (bf16, CUDA)."""
         from .kernels.ops import block_ell_gate_up, block_ell_linear
         T = x.shape[0]
-        _, Tc, _ = self._chunking(T)
+        _, Tc, per = self._chunking(T)
         h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, x.device)
+        cap = self.grid_cap(x.device)
+        own = (self.rank * per, (self.rank + 1) * per)  # this rank's rows of every chunk
+        fold = add_residual and self._can_fold(per)
 
         def partial_fn(xi: torch.Tensor, dst: torch.Tensor) -> None:
-            block_ell_gate_up(xi, self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h)
-            block_ell_linear(h, self.vd, self.cd, out=dst)
+            block_ell_gate_up(xi, self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h, max_ctas=cap)
+            # the residual goes into this rank's own rows only, so the sum over ranks adds it once
+            block_ell_linear(h, self.vd, self.cd, out=dst, residual=xi if fold else None,
+                             residual_rows=own if fold else None, max_ctas=cap)
 
-        return self.run_chunks(x, partial_fn, out, add_residual)
+        return self.run_chunks(x, partial_fn, out, add_residual=add_residual and not fold)
+
+    def _can_fold(self, per: int) -> bool:
+        """Whether the down kernel can add the residual to this rank's rows: at
+        tile size 128 its work units are 256-token tiles, so the rows must
+        start on such a tile."""
+        return self.B != 128 or per % 256 == 0
 
     def forward_host(self, x_own: torch.Tensor, out_host: torch.Tensor = None, add_residual: bool = True,
                      device=None) -> torch.Tensor:
@@ -145,6 +196,9 @@ class ShardedSwiGLU:
         xfull = [self._buf(f"xf{i}", (Tc, d), torch.bfloat16, dev) for i in range(2)]
         partial = [self._buf(f"p{i}", (Tc, d), torch.bfloat16, dev) for i in range(2)]
         h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, dev)
+        cap = self.grid_cap(dev)
+        own = (self.rank * per, (self.rank + 1) * per)
+        fold = add_residual and self._can_fold(per)
         cur = torch.cuda.current_stream(dev)
         s_in = self._stream("in", dev)
         s_out = self._stream("out", dev)
@@ -171,15 +225,16 @@ class ShardedSwiGLU:
             g_cur.wait()
             if i >= 2:
                 works[i - 2].wait()  # partial buffer i%2 is free again
-            block_ell_gate_up(xfull[i % 2], self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h)
-            block_ell_linear(h, self.vd, self.cd, out=partial[i % 2])
+            block_ell_gate_up(xfull[i % 2], self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h, max_ctas=cap)
+            block_ell_linear(h, self.vd, self.cd, out=partial[i % 2], residual=xfull[i % 2] if fold else None,
+                             residual_rows=own if fold else None, max_ctas=cap)
             done[i] = torch.cuda.Event()
             done[i].record(cur)
             works.append(dist.reduce_scatter_tensor(out[i * per:(i + 1) * per], partial[i % 2],
                                                     op=dist.ReduceOp.SUM, group=self.group, async_op=True))
             with torch.cuda.stream(s_out):
                 works[i].wait()  # s_out waits for this chunk's reduce-scatter
-                if add_residual:
+                if add_residual and not fold:
                     out[i * per:(i + 1) * per].add_(xs[i * per:(i + 1) * per])
                 out_host[i * per:(i + 1) * per].copy_(out[i * per:(i + 1) * per], non_blocking=True)
         for w in works:
@@ -196,13 +251,14 @@ class ShardedSwiGLU:
             self._bufs[key] = st
         return st
 
-    def run_chunks(self, x: torch.Tensor, partial_fn, out: torch.Tensor = None, add_residual: bool = True,
+    def run_chunks(self, x: torch.Tensor, partial_fn, out: torch.Tensor = None, add_residual: bool = False,
                    dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
         """The chunk pipeline of ``forward`` around any partial computation:
         ``partial_fn(x_chunk, dst)`` writes this rank's partial ``[Tc, d_model]``
         for a token chunk; the reduce-scatter of chunk i runs (async) while
-        chunk i+1 computes, two partial buffers alternate, and the residual is
-        added on the owned rows at the end."""
+        chunk i+1 computes and two partial buffers alternate.  ``add_residual``
+        adds x on the owned rows at the end, for a ``partial_fn`` that leaves
+        the residual out."""
         import torch.distributed as dist
         T = x.shape[0]
         n, Tc, per = self._chunking(T)

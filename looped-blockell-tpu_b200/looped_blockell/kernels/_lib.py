@@ -36,13 +36,15 @@ class BellFFNDesc(C.Structure):
     _fields_ = [("T", C.c_int64), ("d_model", C.c_int32), ("d_ff", C.c_int32), ("dtype", C.c_int32),
                 ("add_residual", C.c_int32), ("x", C.c_void_p), ("residual", C.c_void_p), ("h", C.c_void_p),
                 ("gate_pre", C.c_void_p), ("up_out", C.c_void_p), ("out", C.c_void_p), ("plan", C.c_void_p),
-                ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p)]
+                ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p),
+                ("max_ctas", C.c_int32), ("reserved", C.c_int32)]
 
 
 class BellLinearDesc(C.Structure):
     _fields_ = [("T", C.c_int64), ("dtype", C.c_int32), ("out_dtype", C.c_int32), ("add_residual", C.c_int32),
-                ("reserved", C.c_int32), ("x", C.c_void_p), ("residual", C.c_void_p), ("out", C.c_void_p),
-                ("plan", C.c_void_p), ("w", BellEll), ("status", C.c_void_p)]
+                ("max_ctas", C.c_int32), ("x", C.c_void_p), ("residual", C.c_void_p), ("out", C.c_void_p),
+                ("plan", C.c_void_p), ("w", BellEll), ("status", C.c_void_p), ("residual_row_lo", C.c_int64),
+                ("residual_row_hi", C.c_int64)]
 
 
 class BellTernaryEll(C.Structure):
@@ -62,7 +64,13 @@ class BellLoopDesc(C.Structure):
     _fields_ = [("T", C.c_int64), ("d_model", C.c_int32), ("d_ff", C.c_int32), ("L", C.c_int32),
                 ("eps", C.c_float), ("h_in", C.c_void_p), ("h_out", C.c_void_p), ("norm_gain", C.c_void_p),
                 ("hn", C.c_void_p), ("h_mid", C.c_void_p), ("plan", C.c_void_p), ("barrier", C.c_void_p),
-                ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p)]
+                ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p),
+                ("mode", C.c_int32), ("reserved", C.c_int32)]
+
+
+BELL_LOOP_AUTO = 0
+BELL_LOOP_LAUNCHES = 1
+BELL_LOOP_PERSISTENT = 2
 
 
 class BellDownBwdDesc(C.Structure):

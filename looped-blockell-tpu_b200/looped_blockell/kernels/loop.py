@@ -13,9 +13,19 @@ from . import _lib
 from .ops import TILE_IN_OUT, _check_cuda, _ell, _prep_ell, _stream, plan_bytes, rmsnorm
 
 
+LOOP_AUTO = _lib.BELL_LOOP_AUTO
+LOOP_LAUNCHES = _lib.BELL_LOOP_LAUNCHES
+LOOP_PERSISTENT = _lib.BELL_LOOP_PERSISTENT
+
+
 def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, L: int,
-               eps: float = 1e-5, layout: int = TILE_IN_OUT, out: torch.Tensor = None) -> torch.Tensor:
-    """L iterations of ``h = h + FFN(RMSNorm(h))`` with one weight set (bf16)."""
+               eps: float = 1e-5, layout: int = TILE_IN_OUT, out: torch.Tensor = None,
+               mode: int = LOOP_AUTO) -> torch.Tensor:
+    """L iterations of ``h = h + FFN(RMSNorm(h))`` with one weight set (bf16).
+
+    ``mode`` picks the implementation: ``LOOP_AUTO`` (the library's fastest),
+    ``LOOP_LAUNCHES`` (1 + 3L kernel launches) or ``LOOP_PERSISTENT`` (one
+    persistent kernel, tile size 64)."""
     lib = _lib.load()
     _check_cuda("h", h)
     if h.dim() != 2 or h.dtype != torch.bfloat16:
@@ -47,6 +57,7 @@ def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, 
     desc.up = _ell(vu, cu, d // B, layout)
     desc.down = _ell(vd, cd, F // B, layout)
     desc.status = None
+    desc.mode = int(mode)
     with torch.cuda.device(dev):
         _lib.check(lib.bell_loop_fwd_bf16(C.byref(desc), _stream()), "looped_ffn")
     return out

@@ -110,9 +110,11 @@ def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layo
     return out, h, gate_pre, up_out
 
 
-def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: int = TILE_IN_OUT, h=None):
+def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: int = TILE_IN_OUT, h=None,
+                      max_ctas: int = 0):
     """First half only: ``h = silu(x Wg) * (x Wu)`` (the down weight is only
-    shape-checked).  Used by the d_ff-sharded forward."""
+    shape-checked).  Used by the d_ff-sharded forward.  ``max_ctas`` caps the
+    persistent grid (0 = every SM), leaving SMs to a concurrent collective."""
     lib = _lib.load()
     _check_cuda("x", x)
     if x.dim() != 2 or x.dtype != torch.bfloat16:
@@ -134,6 +136,7 @@ def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: 
     desc.gate = _ell(vg, cg, d_model // B, layout)
     desc.up = _ell(vu, cu, d_model // B, layout)
     desc.down = _ell(vd, cd, d_ff // vd.shape[2], layout)
+    desc.max_ctas = int(max_ctas)
     with torch.cuda.device(x.device):
         _lib.check(lib.bell_gate_up_bf16(C.byref(desc), _stream()), "block_ell_gate_up")
     return h
@@ -160,8 +163,12 @@ def block_ell_swiglu_fwd_with_intermediate(x, v_gate, ci_gate, v_up, ci_up, v_do
 
 def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, residual: Optional[torch.Tensor] = None,
                      out_dtype: Optional[torch.dtype] = None, layout: int = TILE_IN_OUT,
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``y = x @ W^T (+ residual)`` for one Block-ELL weight; x is [N, C*B]."""
+                     out: Optional[torch.Tensor] = None, residual_rows: Optional[Sequence[int]] = None,
+                     max_ctas: int = 0) -> torch.Tensor:
+    """``y = x @ W^T (+ residual)`` for one Block-ELL weight; x is [N, C*B].
+
+    bf16 only: ``residual_rows=(lo, hi)`` adds the residual to output rows
+    [lo, hi) only, and ``max_ctas`` caps the persistent grid (0 = every SM)."""
     lib = _lib.load()
     _check_cuda("x", x)
     if x.dim() != 2:
@@ -195,6 +202,17 @@ def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, 
     desc.residual = residual.data_ptr() if residual is not None else None
     desc.w = _ell(v, c, in_f // B, layout)
     desc.status = None
+    desc.max_ctas = int(max_ctas)
+    if residual_rows is not None:
+        if dtype != torch.bfloat16:
+            raise RuntimeError("residual_rows needs bf16 inputs")
+        lo, hi = (int(v_) for v_ in residual_rows)
+        if not 0 <= lo <= hi <= N:
+            raise RuntimeError(f"residual_rows {(lo, hi)} outside [0, {N}]")
+        if lo == hi:
+            desc.add_residual = 0
+        else:
+            desc.residual_row_lo, desc.residual_row_hi = lo, hi
     fn = lib.bell_linear_bf16 if dtype == torch.bfloat16 else lib.bell_linear_f32
     with torch.cuda.device(x.device):
         _lib.check(fn(C.byref(desc), _stream()), "block_ell_linear")

@@ -36,7 +36,7 @@ def test_every_declared_symbol_is_exported():
 
 def test_abi_version_and_plan_bytes():
     lib = _lib().load()
-    assert lib.bell_abi_version() == 1
+    assert lib.bell_abi_version() == 2
     # gate/up: 128 rows x (8+8) entries, counts; down: 32 x 32, counts — 16-byte aligned sections
     assert lib.bell_plan_bytes(128, 8, 8, 32, 32) == 128 * 16 * 4 + 128 * 4 + 32 * 32 * 4 + 32 * 4
     assert lib.bell_plan_bytes(0, 0, 0, 3, 5) % 16 == 0

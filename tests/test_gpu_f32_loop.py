@@ -77,15 +77,24 @@ def test_loop_golden_fixture():
     assert O.rel_l2(out.float().cpu().numpy(), z["out"]) < TOL_BF16
 
 
-def test_loop_config4_row_sample():
+LOOP_MODES = ["auto", "launches", "persistent"]
+
+
+def _mode(name):
+    from looped_blockell.kernels import loop as kl
+    return {"auto": kl.LOOP_AUTO, "launches": kl.LOOP_LAUNCHES, "persistent": kl.LOOP_PERSISTENT}[name]
+
+
+@pytest.mark.parametrize("mode", LOOP_MODES)
+def test_loop_config4_row_sample(mode):
     """BASELINE config 4 (L=8, T=8192, d=1024, F=4096, B=64, 25%) vs the oracle
-    on a 512-token sample."""
+    on a 512-token sample, for each loop implementation."""
     from looped_blockell.synth import CONFIGS, make_ffn
     K = _K()
     cfg = CONFIGS[4]
     c = make_ffn(cfg, device="cuda")
     gain = torch.ones(cfg.d_model, dtype=torch.bfloat16, device="cuda")
-    out = K.looped_ffn(c["x"], gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L)
+    out = K.looped_ffn(c["x"], gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L, mode=_mode(mode))
     rows = np.random.default_rng(1).choice(cfg.T, 512, replace=False)
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
     ref = O.looped_ffn(f(c["x"])[rows], np.ones(cfg.d_model), (f(c["vg"]), c["cg"].cpu().numpy(), 0),
@@ -97,18 +106,20 @@ def test_loop_config4_row_sample():
     assert K.read_status() == 0
 
 
+@pytest.mark.parametrize("mode", LOOP_MODES)
 @pytest.mark.parametrize("layout", [O.LAYOUT_IN_OUT, O.LAYOUT_OUT_IN])
 @pytest.mark.parametrize("T,L,dead", [(200, 3, 0), (77, 2, 6), (384, 5, 3)])
-def test_loop_edge_cases(layout, T, L, dead):
+def test_loop_edge_cases(layout, T, L, dead, mode):
     """Ragged token counts (partial 128-token tiles), dead slots, non-unit
-    gain, both tile layouts: the single persistent loop kernel vs the oracle
-    with the bf16 roundings of the op."""
+    gain, both tile layouts, each loop implementation (the library's default,
+    the per-phase launches, the single persistent kernel) vs the oracle with
+    the bf16 roundings of the op."""
     K = _K()
     case = make_case(T, 256, 512, 64, 2, 3, 4, seed=T + L, dead=dead)
     dev = to_dev(case, torch.bfloat16, layout)
     gain = (1.0 + 0.25 * torch.randn(256, generator=torch.Generator().manual_seed(L))).to(torch.bfloat16)
     out = K.looped_ffn(dev["x"], gain.cuda(), dev["vg"], dev["cg"], dev["vu"], dev["cu"], dev["vd"], dev["cd"], L=L,
-                       layout=layout)
+                       layout=layout, mode=_mode(mode))
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
     vt = (lambda t: np.swapaxes(f(t), -1, -2)) if layout == O.LAYOUT_OUT_IN else f
     ref = O.looped_ffn(f(dev["x"]), f(gain), (vt(dev["vg"]), case["cg"], 0), (vt(dev["vu"]), case["cu"], 0),
