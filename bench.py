@@ -207,6 +207,8 @@ def main():
     ap.add_argument("--sm-reserve", type=int, default=None,
                     help="N>1: SMs kept out of the GEMM grids for NCCL (default BELL_SM_RESERVE or 16)")
     ap.add_argument("--chunks", type=int, default=4, help="N>1: token chunks of the reduce-scatter pipeline")
+    ap.add_argument("--loop-mode", default="auto", choices=["auto", "launches", "persistent"],
+                    help="config 4: the loop implementation")
     ap.add_argument("--nccl-max-ctas", type=int, default=None,
                     help="N>1: NCCL CTA cap (default: the SM reserve)")
     ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd", "convert"],
@@ -486,10 +488,15 @@ def run_gpu(args, cfg, rank, world):
         out = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
         h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
         gain = torch.ones(d, dtype=torch.bfloat16, device="cuda")
-        launches_per_step = 1 + 3 * cfg.L  # plan, then RMSNorm + gate/up + down per iteration
+        from looped_blockell.kernels import loop as kl
+        mode = {"auto": kl.LOOP_AUTO, "launches": kl.LOOP_LAUNCHES, "persistent": kl.LOOP_PERSISTENT}[args.loop_mode]
+        persistent = kl.loop_uses_persistent(mode, cfg.B)
+        # copy h_in, plan, then one persistent kernel (+ its counter reset) or RMSNorm + gate/up + down per iteration
+        launches_per_step = 2 if persistent else 1 + 3 * cfg.L
 
         def step(x):
-            return looped_ffn(x, gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L, layout=lay)
+            return looped_ffn(x, gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L, layout=lay,
+                              mode=mode)
     else:
         out = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
         h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
@@ -668,7 +675,9 @@ def run_gpu(args, cfg, rank, world):
                                 "traffic_source": GU_DRAM_NOTE.get(args.config) if traffic else None,
                                 "kernel_ms": gu["ms"], "whole_step_frac": tflops / world / tc_peak}
         if cfg.L > 1:  # the whole loop step (gate/up and down kernels dominate)
-            line["roofline"] = {"bound": "tensor", "kernel": "loop step (bell_bf16_kernel gate/up + down)", "achieved": tflops,
+            line["config"]["loop_mode"] = args.loop_mode + (" (persistent kernel)" if persistent else " (launches)")
+            line["roofline"] = {"bound": "tensor", "kernel": "loop step (" + ("loop_kernel, one persistent launch"
+                                if persistent else "bell_bf16_kernel gate/up + down launches") + ")", "achieved": tflops,
                                 "peak": tc_peak, "unit": "TFLOP/s", "frac": tflops / tc_peak,
                                 "peak_source": f"{peak_src} bf16 burst", "traffic": None, "kernel_ms": ms}
         if world == 1 and not args.no_cpu:

@@ -223,12 +223,17 @@ int bell_swiglu_fwd_ternary(const BellTernaryFFNDesc* desc, void* stream);
 /* ------------------------------------------------------------------- loop */
 
 /*
- * L shared-weight iterations of  h <- h + FFN(RMSNorm(h))  in one persistent
- * kernel (bf16).  Replaces titan::persistent_mlp_step's per-block host loop
- * (csrc/loop/persistent_core.cu:273-337, loop_ops.cpp:52-66) for the
+ * L shared-weight iterations of  h <- h + FFN(RMSNorm(h))  (bf16), as one
+ * persistent kernel (BELL_LOOP_PERSISTENT) or stream-ordered kernel launches
+ * (BELL_LOOP_LAUNCHES).  Replaces titan::persistent_mlp_step's per-block host
+ * loop (csrc/loop/persistent_core.cu:273-337, loop_ops.cpp:52-66) for the
  * shared-weight case.  h_in, h_out: [T, d_model]; norm_gain: [d_model] bf16;
  * workspaces: hn [T, d_model] bf16, h_mid [T, d_ff] bf16, plan, and
- * `barrier` (>= 64 bytes, zero-filled by the library on each call).
+ * `workspace` (bell_loop_workspace_bytes() bytes, 16-byte aligned).  At tile
+ * size 64 the RMSNorm is folded into the GEMMs: the gain multiplies the
+ * gate/up tiles (copies in the workspace), the down epilogue keeps per-row
+ * sums of squares of the new state, and the gate/up epilogue scales each
+ * token row by its 1/rms; other tile sizes run a separate RMSNorm kernel.
  */
 typedef struct BellLoopDesc {
   int64_t T;
@@ -241,7 +246,7 @@ typedef struct BellLoopDesc {
   void* hn;
   void* h_mid;
   void* plan;
-  void* barrier;
+  void* workspace;             /* bell_loop_workspace_bytes() bytes          */
   BellEll gate, up, down;
   int32_t* status;
   int32_t mode;                /* BELL_LOOP_*                                 */
@@ -256,6 +261,8 @@ enum {
 };
 
 int bell_loop_fwd_bf16(const BellLoopDesc* desc, void* stream);
+size_t bell_loop_workspace_bytes(int64_t T, int32_t d_model, int32_t R_gu, int32_t K_gate, int32_t K_up,
+                                 int32_t B);
 
 /* Diagonal SSM injection h = exp(-softplus(log_dt) exp(log_A)) h + softplus(log_dt) e
  * (bf16 h/e, fp32 log_A/log_dt [d]); replaces diagonal_injection_cuda

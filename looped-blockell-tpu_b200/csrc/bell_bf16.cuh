@@ -44,7 +44,64 @@ struct Bf16Params {
   uint64_t timeout_ns;
   int32_t max_ctas;  // cap on the persistent grid (0 = all SMs)
   int64_t res_lo, res_hi;  // linear: residual added to token rows [res_lo, res_hi) only
+  // Token-tile dataflow (the persistent loop kernel; NULL elsewhere): before a
+  // unit of token tile m loads its activations, the producer waits until
+  // dep_cnt[m] >= dep_target; after a unit's stores, each epilogue warp adds 1
+  // to sig_cnt[m].
+  const unsigned* dep_cnt;
+  unsigned dep_target;
+  unsigned* sig_cnt;
+  // the epilogue also waits for epi_dep_cnt[m] >= epi_dep_target (and for
+  // dep_cnt[m] >= dep_target) before it reads global inputs of tile m
+  const unsigned* epi_dep_cnt;
+  unsigned epi_dep_target;
+  // RMSNorm folded into the GEMMs (the loop at tile size 64, NULL elsewhere):
+  // a gate/up epilogue scales row t's accumulators by
+  // rsqrt(sum(row_ss[t*ss_parts .. +ss_parts]) * inv_d + eps) before SiLU*up;
+  // a linear epilogue writes the sum of squares of row t's stored (bf16)
+  // outputs of block-row r to ss_out[t*ss_parts + r].
+  const float* row_ss;
+  float* ss_out;
+  int32_t ss_parts;
+  float inv_d, eps;
+  // segment of the unit sequence this launch (or loop-kernel phase) covers:
+  // units [u_begin, u_end) of the n_mtiles * R (u_end == 0: all of them)
+  int32_t u_begin, u_end;
 };
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait (bounded) until *cnt >= target; the acquire and the proxy fence that
+// follows order this thread's later loads, TMA loads included, after the
+// writes the counter publishes.  Returns false on timeout or abort.
+__device__ __forceinline__ bool wait_count(const unsigned* cnt, unsigned target, const Ctl& ctl) {
+  if (ld_acquire_u32(cnt) < target) {
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_u32(cnt) < target) {
+      if (*ctl.abort) return false;
+      if (globaltimer_ns() - t0 > ctl.timeout_ns) {
+        raise_status(ctl, BELL_STATUS_TIMEOUT);
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
+
+// Publish this warp's global stores (generic proxy, read later by TMA in
+// other CTAs) and add one to *cnt.
+__device__ __forceinline__ void signal_count(unsigned* cnt) {
+  fence_proxy_async_global();
+  __threadfence();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) atomicAdd(cnt, 1u);
+}
 
 // Whether token row `row` gets the residual: res_hi == 0 means every row.
 __device__ __forceinline__ bool res_row(const Bf16Params& p, int64_t row) {

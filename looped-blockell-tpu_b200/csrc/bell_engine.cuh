@@ -5,7 +5,8 @@
 // A phase multiplies 128-token activation tiles by the Block-ELL tiles of
 // one matrix (gate/up together, or one linear matrix).  A work unit is
 // (token tile m, output block-row r); the CTA walks units
-// u = blockIdx.x + i * gridDim.x and its i-th unit (counted across phases)
+// u = blockIdx.x + i * gridDim.x (of a segment [u_begin, u_end) of the
+// phase when one is set) and its i-th unit (counted across phases)
 // goes to MMA issuer i & 1.  Warp roles:
 //   warps 0, 6, 7, 8  TMA producers: 0/6 fill ring 0, 7/8 fill ring 1; the
 //                     two of a ring take its stage uses alternately.  Each
@@ -177,6 +178,22 @@ __device__ __forceinline__ int local_units(int n_units) {
   return int(blockIdx.x) < n_units ? (n_units - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x) : 0;
 }
 
+// This CTA's units of the segment [u_begin, u_end) of a phase: the ordinals
+// i of u = blockIdx.x + i * gridDim.x inside the segment start at seg_lo and
+// number seg_count; unit_at gives the i-th of them.
+__device__ __forceinline__ int seg_lo(const Bf16Params& p) {
+  const int b = p.u_begin - int(blockIdx.x);
+  return b <= 0 ? 0 : (b + int(gridDim.x) - 1) / int(gridDim.x);
+}
+__device__ __forceinline__ int seg_count(const Bf16Params& p) {
+  const int hi = local_units(p.u_end > 0 ? p.u_end : p.n_mtiles * p.R);
+  const int lo = seg_lo(p);
+  return hi > lo ? hi - lo : 0;
+}
+__device__ __forceinline__ int unit_at(const Bf16Params& p, int i) {
+  return int(blockIdx.x) + (seg_lo(p) + i) * int(gridDim.x);
+}
+
 // ------------------------------------------------------------------ producer
 // One producer warp for one phase.  `i_base` = units this CTA took in
 // earlier phases.  Returns false (warp-uniform) when a wait gave up.
@@ -187,25 +204,29 @@ __device__ bool produce(const Bf16Params& p, const CUtensorMap* ta, const CUtens
   constexpr int KC = B / kBK;  // stages per plan step
   const int ring = pid >> 1, sub = pid & 1;
   uint32_t* row = s.rows + pid * kRowMax;
-  const int n_units = p.n_mtiles * p.R;
-  const int nl = local_units(n_units);
+  const int nl = seg_count(p);
   const int i0 = (ring - i_base) & 1;
   RowAhead ahead;
   if (i0 < nl) {
     int m0, r0;
-    unit_mr(blockIdx.x + i0 * gridDim.x, p, m0, r0);
+    unit_mr(unit_at(p, i0), p, m0, r0);
     row_fetch(ahead, p.plan, p.counts, p.S, r0);
   }
   for (int i = i0; i < nl; i += 2) {
     int m, r;
-    unit_mr(blockIdx.x + i * gridDim.x, p, m, r);
+    unit_mr(unit_at(p, i), p, m, r);
     const int real = (ahead.cnt & 0xFFFF) * KC;
     row_put(ahead, row, p.S);
     __syncwarp();
     if (i + 2 < nl) {
       int m2, r2;
-      unit_mr(blockIdx.x + (i + 2) * gridDim.x, p, m2, r2);
+      unit_mr(unit_at(p, i + 2), p, m2, r2);
       row_fetch(ahead, p.plan, p.counts, p.S, r2);
+    }
+    if (p.dep_cnt) {  // dataflow: this token tile's activations must be complete
+      bool ok = true;
+      if (elect_one()) ok = wait_count(p.dep_cnt + m, p.dep_target, ctl);
+      if (!__all_sync(0xffffffffu, ok)) return false;
     }
     const int uses = real > 1 ? real : 1;  // a unit without live steps: one empty stage
     for (int j = 0; j < uses; ++j, ++st.g) {
@@ -278,7 +299,7 @@ __device__ bool issue(const Bf16Params& p, const Smem& s, uint32_t tmem, IssueSt
   const uint64_t a_desc0 = sdesc_sw128(smem_u32(s.stages), 16, 1024);
   const uint64_t b_desc0 = W_MN ? sdesc_sw128(smem_u32(s.stages) + G::A_BYTES, 8192, 1024)
                                 : sdesc_sw128(smem_u32(s.stages) + G::A_BYTES, 16, 1024);
-  const int nl = local_units(p.n_mtiles * p.R);
+  const int nl = seg_count(p);
   for (int i = (k - i_base) & 1; i < nl; i += 2) {
     const int ik = (i_base + i) >> 1;  // units of this issuer so far
     const int buf = G::NBUF == 2 ? (ik & 1) : 0;
@@ -383,20 +404,20 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
   constexpr bool TSTORE = SB && B == 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
-  const int nl = local_units(p.n_mtiles * p.R);
+  const int nl = seg_count(p);
   int cw_next = 0;  // count word of the next unit, loaded one unit ahead
   if (nl > 0) {
     int m0, r0;
-    unit_mr(blockIdx.x, p, m0, r0);
+    unit_mr(unit_at(p, 0), p, m0, r0);
     cw_next = p.counts[r0];
   }
   for (int i = 0; i < nl; ++i) {
     int m, r;
-    unit_mr(blockIdx.x + i * gridDim.x, p, m, r);
+    unit_mr(unit_at(p, i), p, m, r);
     const int cw = cw_next;
     if (i + 1 < nl) {
       int m2, r2;
-      unit_mr(blockIdx.x + (i + 1) * gridDim.x, p, m2, r2);
+      unit_mr(unit_at(p, i + 1), p, m2, r2);
       cw_next = p.counts[r2];
     }
     const int iG = i_base + i;
@@ -423,7 +444,7 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
             __syncwarp();
           }
           int m2, r2;
-          unit_mr(blockIdx.x + (i + 1) * gridDim.x, p, m2, r2);
+          unit_mr(unit_at(p, i + 1), p, m2, r2);
           stage_gate_up<B, G>(p, s, m2, r2, q, lane, (i + 1) & 1);
         }
         cp_async_commit();
@@ -433,6 +454,28 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
         cp_async_commit();
       }
       gu_row = s.epi + (q * G::EPI_NSLOT + (G::EPI_NSLOT == 2 ? (i & 1) : 0)) * G::EPI_SLOT + lane * (B * 2);
+    }
+    // dataflow: this thread's own acquire of the writes it is about to read
+    // (the sums of squares, the residual) before touching them; done while
+    // the unit's MMAs run
+    if (p.dep_cnt && !__all_sync(0xffffffffu, wait_count(p.dep_cnt + m, p.dep_target, ctl))) return false;
+    if (p.epi_dep_cnt && !__all_sync(0xffffffffu, wait_count(p.epi_dep_cnt + m, p.epi_dep_target, ctl))) return false;
+    // folded RMSNorm (GU): 1 / rms of this token row from the partial sums of
+    // squares (independent loads, four partial sums, a fixed order)
+    float rs = 1.f;
+    if (GU && p.row_ss && row_ok) {
+      const float* sp = p.row_ss + row * p.ss_parts;
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      int k2 = 0;
+#pragma unroll 4
+      for (; k2 + 4 <= p.ss_parts; k2 += 4) {
+        a4[0] += sp[k2];
+        a4[1] += sp[k2 + 1];
+        a4[2] += sp[k2 + 2];
+        a4[3] += sp[k2 + 3];
+      }
+      for (; k2 < p.ss_parts; ++k2) a4[0] += sp[k2];
+      rs = rsqrtf(((a4[0] + a4[1]) + (a4[2] + a4[3])) * p.inv_d + p.eps);
     }
     // warp-uniform before the collective tcgen05.ld
     if (!__all_sync(0xffffffffu, mbar_wait(&s.acc_full[ab], use & 1u, ctl))) {
@@ -446,6 +489,7 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
     const bool any0 = (cw >> 16) & 1;
     const bool any1 = (cw >> 17) & 1;
     if constexpr (SB && G::EPI_NSLOT == 1) cp_async_wait_group<0>();
+    float ssq = 0.f;  // linear: squares of this row's stored outputs (folded RMSNorm of the next step)
     const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t((k * G::NBUF + buf) * G::ACC_COLS);
 #pragma unroll 1
     for (int j = 0; j < B / 32; ++j) {
@@ -462,8 +506,8 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
         uint32_t hp[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const float g0 = __uint_as_float(g[2 * t]), g1 = __uint_as_float(g[2 * t + 1]);
-          const float u0 = __uint_as_float(v[2 * t]), u1 = __uint_as_float(v[2 * t + 1]);
+          const float g0 = __uint_as_float(g[2 * t]) * rs, g1 = __uint_as_float(g[2 * t + 1]) * rs;
+          const float u0 = __uint_as_float(v[2 * t]) * rs, u1 = __uint_as_float(v[2 * t + 1]) * rs;
           hp[t] = pack_bf16x2(silu_fast(g0) * u0, silu_fast(g1) * u1);
         }
         if (row_ok) {
@@ -548,17 +592,27 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
                            __float_as_uint(f[4 * t + 2]), __float_as_uint(f[4 * t + 3]));
           } else {
             __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + off;
+            uint32_t ow[16];
 #pragma unroll
-            for (int t = 0; t < 4; ++t)
-              st_global_v4(orow + t * 8, pack_bf16x2(f[8 * t], f[8 * t + 1]), pack_bf16x2(f[8 * t + 2], f[8 * t + 3]),
-                           pack_bf16x2(f[8 * t + 4], f[8 * t + 5]), pack_bf16x2(f[8 * t + 6], f[8 * t + 7]));
+            for (int t = 0; t < 16; ++t) ow[t] = pack_bf16x2(f[2 * t], f[2 * t + 1]);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) st_global_v4(orow + t * 8, ow[4 * t], ow[4 * t + 1], ow[4 * t + 2], ow[4 * t + 3]);
+            if (p.ss_out) {
+#pragma unroll
+              for (int t = 0; t < 16; ++t) {
+                const float2 r2 = unpack_bf16x2(ow[t]);
+                ssq = fmaf(r2.x, r2.x, fmaf(r2.y, r2.y, ssq));
+              }
+            }
           }
         }
       }
     }
+    if (!GU && p.ss_out && row_ok) p.ss_out[row * p.ss_parts + r] = ssq;
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.acc_empty[ab]);
+    if (p.sig_cnt) signal_count(p.sig_cnt + m);  // dataflow: this warp's rows of the unit are stored
     if constexpr (TSTORE) {  // this warp's 32 rows of d_gate and d_up, out of the staging slot
       const int64_t row0 = int64_t(m) * kBM + q * 32;
       fence_proxy_async_smem();  // the in-place writes above -> visible to the TMA engine

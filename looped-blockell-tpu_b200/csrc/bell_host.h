@@ -62,12 +62,20 @@ int check_ffn(const BellFFNDesc* d, int dtype);
 int launch_ffn_plan(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
 int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
 int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
+
+// Workspace of the loop: per-tile counters, per-row partial sums of squares
+// and the gain-scaled gate/up tiles (tile size 64; other sizes need none).
+struct LoopWs {
+  size_t counters, ss, wg, wu, total;
+};
+LoopWs loop_ws(int64_t T, int32_t d_model, int32_t R_gu, int32_t K_g, int32_t K_u, int32_t B);
 // Weight tensor map of a bf16 Block-ELL matrix: 64 x 64 boxes, 128-byte swizzle.
 int make_w_map(CUtensorMap* m, const BellEll& e);
 
 // The L-iteration loop as one persistent cooperative kernel (tile size 64;
 // bell_loop_kernel.cu).  h_out must already hold h_in and the plan be built.
-int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s);
+int loop_persistent_bf16(const BellLoopDesc* d, const BellEll& wg, const BellEll& wu, int32_t* status,
+                         cudaStream_t s);
 
 // Wait budget for device-side bounded waits (ns).
 uint64_t wait_budget_ns();

@@ -156,6 +156,94 @@ __global__ void __launch_bounds__(256) bell_inject_rmsnorm_kernel(
   }
 }
 
+// Sums of squares of the bf16 state per 64-column block: ss[t*parts + r] =
+// sum_{j<64} h[t, 64r + j]^2 (the folded RMSNorm's input for the first
+// iteration; later iterations get them from the down epilogue).  One warp per
+// row; lane group g = lane/8 takes block r = 4i + g, 8 lanes x 8 columns.
+__global__ void __launch_bounds__(256) bell_row_ss_kernel(const __nv_bfloat16* __restrict__ h, float* __restrict__ ss,
+                                                          int64_t T, int d) {
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const int parts = d / 64;
+  for (int r0 = 0; r0 < parts; r0 += 4) {
+    const int r = r0 + (lane >> 3);
+    float acc = 0.f;
+    if (r < parts) {
+      const uint4 v = *reinterpret_cast<const uint4*>(h + row * d + r * 64 + (lane & 7) * 8);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = unpack_bf16x2(w[t]);
+        acc = fmaf(f.x, f.x, fmaf(f.y, f.y, acc));
+      }
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((lane & 7) == 0 && r < parts) ss[row * parts + r] = acc;
+  }
+}
+
+// out[r,k] = tile (r,k) of w with every input row i scaled by gain[c*64 + i]
+// (c = cols[r,k]): RMSNorm's gain folded into a gate/up weight.  Dead slots
+// keep their tile unscaled (the kernels skip them).
+__global__ void __launch_bounds__(256) bell_gain_scale_kernel(const __nv_bfloat16* __restrict__ w,
+                                                              const int32_t* __restrict__ cols,
+                                                              const __nv_bfloat16* __restrict__ gain,
+                                                              __nv_bfloat16* __restrict__ out, int64_t n8, int C,
+                                                              int out_in) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 8;               // first of 8 elements (one 16-byte group)
+    const int64_t tile = e / (64 * 64);
+    const int within = int(e % (64 * 64));
+    const int c = cols[tile];
+    uint4 v = *reinterpret_cast<const uint4*>(w + e);
+    if (c >= 0 && c < C) {
+      uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      if (out_in) {  // [B_out][B_in]: the 8 elements are consecutive inputs
+        const int i0 = within % 64;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = unpack_bf16x2(u[t]);
+          u[t] = pack_bf16x2(f.x * __bfloat162float(gain[c * 64 + i0 + 2 * t]),
+                             f.y * __bfloat162float(gain[c * 64 + i0 + 2 * t + 1]));
+        }
+      } else {  // [B_in][B_out]: one input row
+        const float gsc = __bfloat162float(gain[c * 64 + within / 64]);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = unpack_bf16x2(u[t]);
+          u[t] = pack_bf16x2(f.x * gsc, f.y * gsc);
+        }
+      }
+      v = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+    *reinterpret_cast<uint4*>(out + e) = v;
+  }
+}
+
+static size_t a16(size_t v) { return (v + 15) & ~size_t(15); }
+
+LoopWs loop_ws(int64_t T, int32_t d_model, int32_t R_gu, int32_t K_g, int32_t K_u, int32_t B) {
+  LoopWs L{};
+  if (B != 64 || T <= 0) {
+    L.total = 64;
+    return L;
+  }
+  const int64_t n_mt = (T + 127) / 128;
+  size_t off = 0;
+  L.counters = off;
+  off += a16(size_t(3 * n_mt) * 4);
+  L.ss = off;
+  off += a16(size_t(T) * size_t(d_model / 64) * 4);
+  L.wg = off;
+  off += a16(size_t(R_gu) * K_g * 64 * 64 * 2);
+  L.wu = off;
+  off += a16(size_t(R_gu) * K_u * 64 * 64 * 2);
+  L.total = off;
+  return L;
+}
+
 int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d, float eps, cudaStream_t s) {
   if (T == 0) return BELL_OK;
   const int64_t blocks = (T + 7) / 8;
@@ -165,12 +253,9 @@ int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d,
   return check_launch("bell_rmsnorm_kernel");
 }
 
-// The loop runs as one launch per phase (RMSNorm, gate/up, down) unless the
-// descriptor asks for the single persistent kernel (bell_loop_kernel.cu; tile
-// size 64, needs the barrier workspace).
-static bool use_persistent_loop(const BellLoopDesc* d) {
-  return d->mode == BELL_LOOP_PERSISTENT;
-}
+// BELL_LOOP_AUTO at tile size 64: the single persistent kernel (true) or the
+// stream-ordered launches (false), whichever measured faster on B200.
+static constexpr bool kAutoPersistent = false;
 
 }  // namespace bell
 
@@ -239,14 +324,10 @@ int bell_diag_injection_bf16(int64_t T, int32_t d_model, const void* h, const vo
 int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
   if (d->L < 0) return fail(BELL_ERR_ARG, "L must be >= 0");
-  if (!d->norm_gain || (d->T > 0 && (!d->h_in || !d->h_out || !d->hn || !d->h_mid || !d->plan)))
-    return fail(BELL_ERR_ARG, "h_in, h_out, norm_gain, hn, h_mid and plan must be non-NULL");
+  if (!d->norm_gain || (d->T > 0 && (!d->h_in || !d->h_out || !d->hn || !d->h_mid || !d->plan || !d->workspace)))
+    return fail(BELL_ERR_ARG, "h_in, h_out, norm_gain, hn, h_mid, plan and workspace must be non-NULL");
   if (d->mode != BELL_LOOP_AUTO && d->mode != BELL_LOOP_LAUNCHES && d->mode != BELL_LOOP_PERSISTENT)
     return fail(BELL_ERR_ARG, "unknown loop mode");
-  if (d->mode == BELL_LOOP_PERSISTENT &&
-      (d->gate.B != 64 || !d->barrier || !aligned16(d->barrier) || !aligned16(d->norm_gain) || d->d_model % 8 != 0))
-    return fail(BELL_ERR_SHAPE, "the persistent loop kernel needs tile size 64, d_model % 8 == 0 and an aligned "
-                                "barrier workspace");
   BellFFNDesc f{};
   f.T = d->T;
   f.d_model = d->d_model;
@@ -263,6 +344,15 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   f.down = d->down;
   f.status = d->status;
   if (int rc = check_ffn(&f, BELL_DTYPE_BF16)) return rc;
+  // The persistent kernel (tile size 64) folds RMSNorm into its GEMMs; the
+  // launch loop runs the RMSNorm kernel (measured faster there: config 4,
+  // 0.856 against 0.869-0.882 ms folded).
+  const bool persistent = d->mode == BELL_LOOP_PERSISTENT || (d->mode == BELL_LOOP_AUTO && kAutoPersistent &&
+                                                              d->gate.B == 64);
+  const bool fold = persistent;
+  if (persistent && d->gate.B != 64) return fail(BELL_ERR_SHAPE, "the persistent loop kernel needs tile size 64");
+  if (fold && (!aligned16(d->workspace) || !aligned16(d->norm_gain) || d->d_model % 64 != 0))
+    return fail(BELL_ERR_ALIGN, "loop: workspace and norm_gain must be 16-byte aligned");
   if (int rc = require_sm100()) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t bytes = size_t(d->T) * d->d_model * 2;
@@ -274,14 +364,43 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   int32_t* status = d->status ? d->status : default_status_ptr();
   if (!status) return BELL_ERR_LAUNCH;
   if (int rc = launch_ffn_plan(&f, status, s)) return rc;
-  if (use_persistent_loop(d)) return loop_persistent_bf16(d, status, s);
-  for (int it = 0; it < d->L; ++it) {
-    if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
-    if (int rc = gate_up_bf16(&f, status, s)) return rc;
-    // out = h_mid Wd + h (the pre-norm state), written in place over h
-    if (int rc = down_bf16(&f, status, s)) return rc;
+  if (!fold) {
+    for (int it = 0; it < d->L; ++it) {
+      if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
+      if (int rc = gate_up_bf16(&f, status, s)) return rc;
+      // out = h_mid Wd + h (the pre-norm state), written in place over h
+      if (int rc = down_bf16(&f, status, s)) return rc;
+    }
+    return BELL_OK;
   }
-  return BELL_OK;
+  // folded RMSNorm: gain into the gate/up tiles, the first sums of squares
+  const LoopWs W = loop_ws(d->T, d->d_model, d->gate.R, d->gate.K, d->up.K, 64);
+  char* ws = static_cast<char*>(d->workspace);
+  float* ss = reinterpret_cast<float*>(ws + W.ss);
+  BellEll wg = d->gate, wu = d->up;
+  wg.values = ws + W.wg;
+  wu.values = ws + W.wu;
+  int sms = 0;
+  if (int rc = device_sm_count(&sms)) return rc;
+  const BellEll* src[2] = {&d->gate, &d->up};
+  const BellEll* dst[2] = {&wg, &wu};
+  for (int k = 0; k < 2; ++k) {
+    const int64_t n8 = int64_t(src[k]->R) * src[k]->K * 64 * 64 / 8;
+    const int64_t grid = (n8 + 255) / 256 < int64_t(sms) * 8 ? (n8 + 255) / 256 : int64_t(sms) * 8;
+    bell_gain_scale_kernel<<<unsigned(grid), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(src[k]->values), src[k]->col_indices,
+        static_cast<const __nv_bfloat16*>(d->norm_gain), static_cast<__nv_bfloat16*>(const_cast<void*>(dst[k]->values)),
+        n8, src[k]->C, src[k]->layout == BELL_TILE_OUT_IN ? 1 : 0);
+    if (int rc = check_launch("bell_gain_scale_kernel")) return rc;
+  }
+  bell_row_ss_kernel<<<unsigned((d->T + 7) / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(d->h_out), ss, d->T,
+                                                               d->d_model);
+  if (int rc = check_launch("bell_row_ss_kernel")) return rc;
+  return loop_persistent_bf16(d, wg, wu, status, s);
+}
+
+size_t bell_loop_workspace_bytes(int64_t T, int32_t d_model, int32_t R_gu, int32_t K_gate, int32_t K_up, int32_t B) {
+  return loop_ws(T, d_model, R_gu, K_gate, K_up, B).total;
 }
 
 }  // extern "C"

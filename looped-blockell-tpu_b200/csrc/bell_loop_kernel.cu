@@ -1,20 +1,36 @@
 // bell_loop_kernel.cu — the L-iteration shared-weight loop in ONE persistent
-// kernel:  for it < L:  hn = RMSNorm(h);  h_mid = silu(hn Wg) * (hn Wu);
+// kernel:  for it < L:  h_mid = silu(RMSNorm(h) Wg) * (RMSNorm(h) Wu);
 //                        h = h_mid Wd + h
 // (the order of the reference persistent_mlp_step, csrc/loop/
 // persistent_core.cu:315-335, with one weight set repeated L times).
 //
-// One CTA per SM (cooperative launch, so every CTA is resident and the
-// grid-wide barriers between phases cannot deadlock).  The two GEMM phases
-// are phases of the token-major engine (bell_engine.cuh) with its warp roles;
-// the TMA rings, TMEM accumulators and per-warp pipeline state carry over
-// from phase to phase.  The RMSNorm phase uses every warp, one token row per
-// warp.  Weight tiles are loaded with an L2 evict-last policy, so the 2.6 MB
-// of gate/up/down tiles (config 4) stay L2-resident across all iterations.
-// Every wait — mbarrier or grid barrier — is bounded by the status/abort
-// machinery of bell_ptx.cuh.
+// One CTA per SM (cooperative launch, so every CTA is resident).  The two
+// GEMM phases of every iteration are phases of the token-major engine
+// (bell_engine.cuh) with its warp roles; the TMA rings, TMEM accumulators and
+// per-warp pipeline state carry over from phase to phase.  RMSNorm has no
+// phase of its own: RMSNorm(h) W = diag(1/rms) h diag(gain) W, so the gate/up
+// GEMMs read h itself against gain-scaled tiles (made by the host entry point)
+// and the epilogue multiplies each token row by its 1/rms, from per-row sums
+// of squares that the down epilogue of the previous iteration wrote next to
+// the new h (the first ones come from a small kernel before this one).
 //
-// Tile size 64, either tile layout; other tile sizes use the multi-launch loop.
+// There is no grid barrier: the FFN is token-local, so each 128-token tile m
+// only waits for its own producers, through two per-tile counters:
+//   gu[m]  +1 per epilogue warp per gate/up unit of tile m (h_mid stored);
+//   dn[m]  +1 per epilogue warp per down unit of tile m (h and its sums of
+//          squares stored).
+// A gate/up unit of iteration `it` loads h[m] once dn[m] >= 4 R_model it; a
+// down unit loads h_mid[m] once gu[m] >= 4 R_ff (it+1).  These conditions also
+// cover the write-after-read hazards of the in-place buffers: a tile's next
+// writer waits, through the chain, for every reader of its previous contents.
+// Epilogues acquire the counters themselves before reading what they publish.
+// Every role works through its phases in order and only waits on work of an
+// earlier phase, and every CTA is resident, so the waits always end; each is
+// still bounded by the status/abort machinery of bell_ptx.cuh.  Weight tiles
+// are loaded with an L2 evict-last policy, so the gate/up/down tiles (config
+// 4: 6.3 MB) stay L2-resident across all iterations.
+//
+// Tile size 64, either tile layout; other tile sizes use the launch loop.
 #include <string>
 
 #include "bell_bf16.cuh"
@@ -33,86 +49,14 @@ struct LoopParams {
   int32_t L, d_model;
   float eps;
   __nv_bfloat16* h;           // state, updated in place
-  __nv_bfloat16* hn;          // normalised state
-  const __nv_bfloat16* gain;  // RMSNorm scale [d_model]
-  unsigned int* gbar;         // grid barrier counter (zeroed by the host)
+  unsigned* cnt_gu;           // per-tile counters [n_mtiles] each (zeroed by the host)
+  unsigned* cnt_dn;
+  int32_t n_seg, seg_tiles;   // waves per iteration, token tiles per wave
   int32_t* status;
   uint64_t timeout_ns;
-  Bf16Params gu;              // hn -> h_mid = silu(hn Wg) * (hn Wu)
+  Bf16Params gu;              // h -> h_mid = silu(RMSNorm(h) Wg) * (RMSNorm(h) Wu)
   Bf16Params dn;              // h_mid -> h = h_mid Wd + h
 };
-
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Grid-wide barrier: every CTA arrives once per call; `target` is the
-// cumulative arrival count to wait for.  Generic-proxy stores made before it
-// (RMSNorm output, epilogue stores) are fenced for the async proxy so the
-// TMA loads of other CTAs after it see them.  Bounded: on timeout it records
-// BELL_STATUS_TIMEOUT.  Returns false (uniformly across the CTA) when this
-// CTA must stop: a role of it failed (`failed`), or the barrier timed out.
-__device__ __forceinline__ bool grid_sync(const LoopParams& p, unsigned target, const Ctl& ctl, bool failed) {
-  fence_proxy_async_global();
-  __threadfence();
-  if (__syncthreads_or(failed || *ctl.abort)) return false;
-  bool timed_out = false;
-  if (threadIdx.x == 0) {
-    __threadfence();  // release this CTA's writes (ordered before it by the CTA barrier)
-    atomicAdd(p.gbar, 1u);
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_gpu(p.gbar) < target) {
-      if (globaltimer_ns() - t0 > ctl.timeout_ns) {
-        raise_status(ctl, BELL_STATUS_TIMEOUT);
-        timed_out = true;
-        break;
-      }
-      __nanosleep(64);
-    }
-    __threadfence();  // acquire side: later loads of the CTA see the other CTAs' writes
-  }
-  if (__syncthreads_or(timed_out)) return false;
-  fence_proxy_async_global();
-  return true;
-}
-
-// One warp per token row: hn = h * rsqrt(mean(h^2) + eps) * gain.
-__device__ __forceinline__ void norm_phase(const LoopParams& p) {
-  const int warps = blockDim.x >> 5;
-  const int lane = threadIdx.x & 31;
-  for (int64_t row = int64_t(blockIdx.x) * warps + (threadIdx.x >> 5); row < p.T;
-       row += int64_t(gridDim.x) * warps) {
-    const __nv_bfloat16* x = p.h + row * p.d_model;
-    float ss = 0.f;
-    for (int i = lane * 8; i < p.d_model; i += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(x + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 f = unpack_bf16x2(w[t]);
-        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / float(p.d_model) + p.eps);
-    __nv_bfloat16* y = p.hn + row * p.d_model;
-    for (int i = lane * 8; i < p.d_model; i += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(x + i);
-      const uint4 g = *reinterpret_cast<const uint4*>(p.gain + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w}, gw[4] = {g.x, g.y, g.z, g.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 f = unpack_bf16x2(w[t]), s = unpack_bf16x2(gw[t]);
-        o[t] = pack_bf16x2(f.x * inv * s.x, f.y * inv * s.y);
-      }
-      *reinterpret_cast<uint4*>(y + i) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
-}
 
 // The engine's role functions are called through these non-inlined wrappers.
 // With the producer, issuer and epilogue of both phases all inlined into one
@@ -137,7 +81,7 @@ __device__ __noinline__ bool loop_epilogue(const Bf16Params& p, const eng::Smem&
 
 template <bool W_MN>
 __global__ void __launch_bounds__(eng::kThreads, 1)
-    loop_kernel(const __grid_constant__ CUtensorMap tm_hn, const __grid_constant__ CUtensorMap tm_hmid,
+    loop_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_hmid,
                 const __grid_constant__ CUtensorMap tm_wg, const __grid_constant__ CUtensorMap tm_wu,
                 const __grid_constant__ CUtensorMap tm_wd, const __grid_constant__ LoopParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -149,7 +93,7 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
   const int pid = eng::producer_id(warp), k = warp == 1 ? 0 : 1;
   const bool leader = elect_one();
   if (warp == 0 && (threadIdx.x & 31) == 0) {
-    prefetch_tmap(&tm_hn);
+    prefetch_tmap(&tm_h);
     prefetch_tmap(&tm_hmid);
     prefetch_tmap(&tm_wg);
     prefetch_tmap(&tm_wu);
@@ -159,37 +103,80 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
   const uint64_t pol_w = policy_evict_last();
   eng::ProdState ps;
   eng::IssueState is;
-  const int nl_gu = eng::local_units(p.gu.n_mtiles * p.gu.R);
-  const int nl_dn = eng::local_units(p.dn.n_mtiles * p.dn.R);
-  const unsigned nG = gridDim.x;
+  // The work runs in waves of `seg_tiles` token tiles: wave w = it * S + s
+  // covers tiles [s * seg_tiles, (s+1) * seg_tiles) of iteration it.  Every
+  // role walks, for w = 0 .. L*S, the gate/up units of wave w, then the down
+  // units of wave w-1: a down wave waits on the gate/up wave before it, with
+  // the next gate/up wave's work in between, and a gate/up wave waits on the
+  // down wave of the same tiles one iteration earlier (S >= 2 waves earlier).
+  // Every unit only waits on units earlier in this one global order.
+  const int S = p.n_seg;
+  const int st = p.seg_tiles;
+  const int n_mt = p.gu.n_mtiles;
+  int base = 0;  // units this CTA took in earlier segments
   bool ok = true;
-  for (int it = 0; it < p.L && ok; ++it) {
-    norm_phase(p);
-    if (!grid_sync(p, unsigned(3 * it + 1) * nG, ctl, false)) {
-      ok = false;
-      break;
-    }
-    const int base = it * (nl_gu + nl_dn);  // units this CTA took in earlier phases
+  for (int w = 0; w <= p.L * S && ok; ++w) {
 #pragma unroll 1
-    for (int ph = 0; ph < 2; ++ph) {
-      bool role_ok = true;
+    for (int part = 0; part < 2 && ok; ++part) {
+      const int wv = part == 0 ? w : w - 1;  // gate/up of wave w, then down of wave w-1
+      if (wv < 0 || wv >= p.L * S) continue;
+      const int it = wv / S, sg = wv % S;
+      const int t0 = sg * st, t1 = (sg + 1) * st < n_mt ? (sg + 1) * st : n_mt;
+      if (t0 >= t1) continue;
+      const bool gu_part = part == 0;
+      Bf16Params q = gu_part ? p.gu : p.dn;
+      q.u_begin = t0 * q.R;
+      q.u_end = t1 * q.R;
+      unsigned* sig = gu_part ? p.cnt_gu : p.cnt_dn;  // signalled once per wave, below
+      // The wave's inputs: every tile of the wave ready before any of its
+      // units load (one parallel acquire per tile instead of one per unit).
+      // Gate/up reads h[m] and its sums of squares (down of the previous
+      // iteration); down reads h_mid[m] (gate/up of this iteration) and the
+      // residual h[m] (down of the previous iteration).
+      if (role == eng::kProducer || role == eng::kEpilogue) {
+        const unsigned tgt_dn = 4u * unsigned(p.dn.R) * unsigned(it);
+        const unsigned tgt_gu = 4u * unsigned(p.gu.R) * unsigned(it + 1);
+        const int lane = threadIdx.x & 31;
+        bool w_ok = true;
+        for (int t = t0 + lane; t < t1; t += 32) {
+          if (gu_part) w_ok = w_ok && wait_count(p.cnt_dn + t, tgt_dn, ctl);
+          else w_ok = w_ok && wait_count(p.cnt_gu + t, tgt_gu, ctl) && wait_count(p.cnt_dn + t, tgt_dn, ctl);
+        }
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        fence_proxy_async_global();  // the issuing lanes' TMA loads after every lane's acquire
+      }
       if (role == eng::kProducer) {
-        role_ok = ph == 0 ? loop_produce<true, W_MN>(p.gu, &tm_hn, &tm_wg, &tm_wu, s, ps, base, pid, ctl, pol_a, pol_w)
-                          : loop_produce<false, W_MN>(p.dn, &tm_hmid, &tm_wd, &tm_wd, s, ps, base + nl_gu, pid, ctl,
-                                                      pol_a, pol_w);
+        ok = gu_part ? loop_produce<true, W_MN>(q, &tm_h, &tm_wg, &tm_wu, s, ps, base, pid, ctl, pol_a, pol_w)
+                     : loop_produce<false, W_MN>(q, &tm_hmid, &tm_wd, &tm_wd, s, ps, base, pid, ctl, pol_a, pol_w);
       } else if (role == eng::kIssuer) {
-        role_ok = ph == 0 ? loop_issue<true, W_MN>(p.gu, s, tmem, is, base, k, leader, ctl)
-                          : loop_issue<false, W_MN>(p.dn, s, tmem, is, base + nl_gu, k, leader, ctl);
+        ok = gu_part ? loop_issue<true, W_MN>(q, s, tmem, is, base, k, leader, ctl)
+                     : loop_issue<false, W_MN>(q, s, tmem, is, base, k, leader, ctl);
       } else {
-        role_ok = ph == 0 ? loop_epilogue<true>(p.gu, s, tmem, base, ctl)
-                          : loop_epilogue<false>(p.dn, s, tmem, base + nl_gu, ctl);
+        ok = gu_part ? loop_epilogue<true>(q, s, tmem, base, ctl) : loop_epilogue<false>(q, s, tmem, base, ctl);
+        if (ok) {
+          // one release per warp and wave: every unit of the wave this warp
+          // stored adds one to its tile's counter
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if ((threadIdx.x & 31) == 0) {
+            const int nu = eng::seg_count(q);
+            for (int i = 0; i < nu; ++i) {
+              int m, r;
+              unit_mr(eng::unit_at(q, i), q, m, r);
+              atomicAdd(sig + m, 1u);
+            }
+          }
+          __syncwarp();
+        }
       }
-      if (!grid_sync(p, unsigned(3 * it + 2 + ph) * nG, ctl, !role_ok)) {
-        ok = false;
-        break;
-      }
+      base += eng::seg_count(q);
     }
   }
+  if (!ok && *ctl.abort == 0) raise_status(ctl, BELL_STATUS_INTERNAL);  // a role stopped: stop the others
   if (role == eng::kProducer && !ok) eng::producer_drain<G>(s, ps, pid);
   if (role == eng::kIssuer) eng::issuer_drain(s, k, leader);
   eng::teardown<G>(tmem);
@@ -199,16 +186,16 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
 
 // Host side of the persistent loop.  Preconditions checked by the caller:
 // bf16 descriptor validated by check_ffn, tile size 64, h_out already holds
-// h_in, plan built.  Returns BELL_ERR_LAUNCH when the cooperative grid cannot
-// be formed (the caller then runs the multi-launch loop).
-int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s) {
+// h_in, plan built, `barrier` holds bell_loop_barrier_bytes(T) bytes.
+int loop_persistent_bf16(const BellLoopDesc* d, const BellEll& g, const BellEll& u, int32_t* status,
+                         cudaStream_t s) {
   using namespace loopk;
-  if (!aligned16(d->norm_gain) || !aligned16(d->hn) || !aligned16(d->h_mid) || !aligned16(d->h_out) ||
-      !aligned16(d->barrier))
+  if (!aligned16(d->h_mid) || !aligned16(d->h_out) || !aligned16(d->workspace))
     return fail(BELL_ERR_ALIGN, "loop buffers must be 16-byte aligned");
-  const BellEll &g = d->gate, &u = d->up, &w = d->down;
-  CUtensorMap m_hn, m_hmid, m_wg, m_wu, m_wd;
-  if (int rc = make_map_2d(&m_hn, d->hn, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64, kBM,
+  const BellEll& w = d->down;
+  CUtensorMap m_h, m_hmid, m_wg, m_wu, m_wd;
+  // the gate/up GEMMs read the pre-norm state h (RMSNorm is folded in)
+  if (int rc = make_map_2d(&m_h, d->h_out, MapType::BF16, d->d_model, d->T, uint64_t(d->d_model) * 2, 64, kBM,
                            Swz::B128))
     return rc;
   if (int rc = make_map_2d(&m_hmid, d->h_mid, MapType::BF16, d->d_ff, d->T, uint64_t(d->d_ff) * 2, 64, kBM,
@@ -225,9 +212,15 @@ int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s)
   p.d_model = d->d_model;
   p.eps = d->eps;
   p.h = static_cast<__nv_bfloat16*>(d->h_out);
-  p.hn = static_cast<__nv_bfloat16*>(d->hn);
-  p.gain = static_cast<const __nv_bfloat16*>(d->norm_gain);
-  p.gbar = static_cast<unsigned int*>(d->barrier);
+  const int64_t n_mt = (d->T + kBM - 1) / kBM;
+  const LoopWs W = loop_ws(d->T, d->d_model, g.R, g.K, u.K, 64);
+  p.cnt_gu = reinterpret_cast<unsigned*>(static_cast<char*>(d->workspace) + W.counters);
+  p.cnt_dn = p.cnt_gu + n_mt;
+  float* ss = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + W.ss);
+  // waves of 8 token tiles, at least two per iteration (see the kernel)
+  p.seg_tiles = n_mt >= 16 ? 8 : int32_t((n_mt + 1) / 2);
+  p.n_seg = int32_t((n_mt + p.seg_tiles - 1) / p.seg_tiles);
+  if (p.n_seg < 2) p.n_seg = 2;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
   Bf16Params& gu = p.gu;  // hn -> h_mid
@@ -241,9 +234,13 @@ int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s)
   gu.counts = reinterpret_cast<const int32_t*>(plan + PL.gu_counts);
   gu.out = d->h_mid;
   gu.ld_out = d->d_ff;
-  gu.band = g.R < 32 ? g.R : 32;  // weight bands stay L2-resident while the token tiles pass
+  gu.band = g.R;  // token-tile-major unit order: tiles become ready, and are consumed, in order
   gu.status = status;
   gu.timeout_ns = p.timeout_ns;
+  gu.row_ss = ss;
+  gu.ss_parts = d->d_model / 64;
+  gu.inv_d = 1.0f / float(d->d_model);
+  gu.eps = d->eps;
   Bf16Params& dn = p.dn;  // h_mid -> h = h_mid Wd + h, in place
   dn.T = d->T;
   dn.n_mtiles = gu.n_mtiles;
@@ -260,6 +257,8 @@ int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s)
   dn.band = w.R;
   dn.status = status;
   dn.timeout_ns = p.timeout_ns;
+  dn.ss_out = ss;
+  dn.ss_parts = gu.ss_parts;
 
   const bool w_mn = g.layout == BELL_TILE_IN_OUT;
   const void* fn = w_mn ? reinterpret_cast<const void*>(&loop_kernel<true>)
@@ -272,8 +271,8 @@ int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s)
   int sms = 0;
   if (int rc = device_sm_count(&sms)) return rc;
   const int grid = sms;  // one CTA per SM: every CTA resident, one TMEM owner per SM
-  e = cudaMemsetAsync(d->barrier, 0, 64, s);
-  if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("loop barrier reset: ") + cudaGetErrorString(e));
+  e = cudaMemsetAsync(p.cnt_gu, 0, size_t(2 * n_mt) * sizeof(unsigned), s);
+  if (e != cudaSuccess) return fail(BELL_ERR_LAUNCH, std::string("loop counters reset: ") + cudaGetErrorString(e));
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(grid));
@@ -286,9 +285,9 @@ int loop_persistent_bf16(const BellLoopDesc* d, int32_t* status, cudaStream_t s)
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (w_mn)
-    e = cudaLaunchKernelEx(&cfg, loop_kernel<true>, m_hn, m_hmid, m_wg, m_wu, m_wd, p);
+    e = cudaLaunchKernelEx(&cfg, loop_kernel<true>, m_h, m_hmid, m_wg, m_wu, m_wd, p);
   else
-    e = cudaLaunchKernelEx(&cfg, loop_kernel<false>, m_hn, m_hmid, m_wg, m_wu, m_wd, p);
+    e = cudaLaunchKernelEx(&cfg, loop_kernel<false>, m_h, m_hmid, m_wg, m_wu, m_wd, p);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
     return fail(BELL_ERR_LAUNCH, std::string("loop kernel launch: ") + cudaGetErrorString(e));

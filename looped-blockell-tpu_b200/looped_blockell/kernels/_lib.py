@@ -63,7 +63,7 @@ class BellTernaryFFNDesc(C.Structure):
 class BellLoopDesc(C.Structure):
     _fields_ = [("T", C.c_int64), ("d_model", C.c_int32), ("d_ff", C.c_int32), ("L", C.c_int32),
                 ("eps", C.c_float), ("h_in", C.c_void_p), ("h_out", C.c_void_p), ("norm_gain", C.c_void_p),
-                ("hn", C.c_void_p), ("h_mid", C.c_void_p), ("plan", C.c_void_p), ("barrier", C.c_void_p),
+                ("hn", C.c_void_p), ("h_mid", C.c_void_p), ("plan", C.c_void_p), ("workspace", C.c_void_p),
                 ("gate", BellEll), ("up", BellEll), ("down", BellEll), ("status", C.c_void_p),
                 ("mode", C.c_int32), ("reserved", C.c_int32)]
 
@@ -109,6 +109,7 @@ SIGNATURES = {
     "bell_linear_f32": (C.c_int, [C.POINTER(BellLinearDesc), C.c_void_p]),
     "bell_swiglu_fwd_ternary": (C.c_int, [C.POINTER(BellTernaryFFNDesc), C.c_void_p]),
     "bell_loop_fwd_bf16": (C.c_int, [C.POINTER(BellLoopDesc), C.c_void_p]),
+    "bell_loop_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     "bell_diag_injection_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                            C.c_void_p, C.c_void_p]),
     "bell_inject_rmsnorm_bf16": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

@@ -18,6 +18,16 @@ LOOP_LAUNCHES = _lib.BELL_LOOP_LAUNCHES
 LOOP_PERSISTENT = _lib.BELL_LOOP_PERSISTENT
 
 
+def loop_uses_persistent(mode: int, B: int) -> bool:
+    """Whether ``looped_ffn`` with ``mode`` and tile size ``B`` runs the
+    single persistent kernel."""
+    return mode == LOOP_PERSISTENT or (mode == LOOP_AUTO and B == 64 and AUTO_PERSISTENT)
+
+
+# LOOP_AUTO's choice at tile size 64 (the library applies the same rule)
+AUTO_PERSISTENT = False
+
+
 def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, L: int,
                eps: float = 1e-5, layout: int = TILE_IN_OUT, out: torch.Tensor = None,
                mode: int = LOOP_AUTO) -> torch.Tensor:
@@ -46,13 +56,14 @@ def looped_ffn(h: torch.Tensor, norm_gain: torch.Tensor, v_gate, ci_gate, v_up, 
     mid = torch.empty((N, F), dtype=torch.bfloat16, device=dev)
     plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
                        dtype=torch.uint8, device=dev)
-    barrier = torch.empty(64, dtype=torch.uint8, device=dev)  # zero-filled by the library
+    ws = torch.empty(int(lib.bell_loop_workspace_bytes(N, d, vg.shape[0], vg.shape[1], vu.shape[1], B)),
+                     dtype=torch.uint8, device=dev)
     desc = _lib.BellLoopDesc()
     desc.T, desc.d_model, desc.d_ff, desc.L, desc.eps = N, d, F, int(L), float(eps)
     desc.h_in, desc.h_out = h.data_ptr(), out.data_ptr()
     gain_keep = norm_gain.to(torch.bfloat16).contiguous()
     desc.norm_gain = gain_keep.data_ptr()
-    desc.hn, desc.h_mid, desc.plan, desc.barrier = hn.data_ptr(), mid.data_ptr(), plan.data_ptr(), barrier.data_ptr()
+    desc.hn, desc.h_mid, desc.plan, desc.workspace = hn.data_ptr(), mid.data_ptr(), plan.data_ptr(), ws.data_ptr()
     desc.gate = _ell(vg, cg, d // B, layout)
     desc.up = _ell(vu, cu, d // B, layout)
     desc.down = _ell(vd, cd, F // B, layout)
