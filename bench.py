@@ -209,6 +209,8 @@ def main():
     ap.add_argument("--chunks", type=int, default=4, help="N>1: token chunks of the reduce-scatter pipeline")
     ap.add_argument("--loop-mode", default="auto", choices=["auto", "launches", "persistent"],
                     help="config 4: the loop implementation")
+    ap.add_argument("--l2-pin", action="store_true",
+                    help="keep the gate/up weight tiles in a persisting-L2 window (bell_pin_l2) while timing")
     ap.add_argument("--nccl-max-ctas", type=int, default=None,
                     help="N>1: NCCL CTA cap (default: the SM reserve)")
     ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd", "convert"],
@@ -456,6 +458,14 @@ def run_gpu(args, cfg, rank, world):
     if lay == ops.TILE_OUT_IN:  # same weights, stored [B_out, B_in]
         for k in ("vg", "vu", "vd"):
             c[k] = c[k].transpose(-1, -2).contiguous()
+    pinned = None
+    if args.l2_pin and cfg.dtype == "bf16":
+        # gate and up tiles in one buffer, so one persisting window covers both
+        from looped_blockell.kernels import loop as kl
+        n_g = c["vg"].numel()
+        pinned = torch.cat([c["vg"].reshape(-1), c["vu"].reshape(-1)])
+        c["vg"], c["vu"] = pinned[:n_g].view(c["vg"].shape), pinned[n_g:].view(c["vu"].shape)
+        kl.pin_weights_l2([pinned])
     T, d, F = cfg.T, cfg.d_model, cfg.d_ff
     launches_per_step = 3
     if world > 1:
@@ -655,7 +665,8 @@ def run_gpu(args, cfg, rank, world):
             "config": {"workload": cfg.name, "T": T, "d_model": d, "d_ff": F, "B": cfg.B, "density": cfg.density,
                        "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
                        "parallelism": f"dff{world}" if world > 1 else "single",
-                       "L": cfg.L, "l2": l2_note,
+                       "L": cfg.L, "l2": l2_note + ("; gate/up tiles in a persisting-L2 window" if pinned is not None
+                                                     else ""),
                        **({"chunks": args.chunks, "sm_reserve": sm_reserve,
                            "nccl_max_ctas": args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve}
                           if world > 1 else {})},
@@ -686,6 +697,9 @@ def run_gpu(args, cfg, rank, world):
                                     "sample": f"{args.cpu_tokens} tokens of {cfg.name} ({dt:.1f} s), numpy "
                                               "restatement of the reference path, scaled linearly"}
         print(json.dumps(line), flush=True)
+    if pinned is not None:
+        from looped_blockell.kernels import loop as kl
+        kl.unpin_weights_l2()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -156,3 +156,27 @@ def test_injection_matches_formula():
     dt = np.log1p(np.exp(ld.astype(np.float64)))
     ref = np.exp(-dt * np.exp(la)) * hb.float().cpu().numpy() + dt * eb.float().cpu().numpy()
     assert O.rel_l2(out.float().cpu().numpy(), ref) < 5e-3
+
+
+def test_l2_pinning_window_keeps_results():
+    """pin_weights_l2 / unpin_weights_l2 (the reference's l2_policy.cu:48-155
+    pair) run on the GPU: a persisting-L2 window over the loop's weights,
+    the loop under it, then the window removed; the results are the same bits
+    as without the window (it changes caching only), also through the titan
+    op names."""
+    from looped_blockell.kernels import loop as kl
+    K = _K()
+    case = make_case(300, 256, 512, 64, 2, 3, 4, seed=31)
+    dev = to_dev(case, torch.bfloat16)
+    gain = torch.ones(256, dtype=torch.bfloat16, device="cuda")
+    args = (dev["x"], gain, dev["vg"], dev["cg"], dev["vu"], dev["cu"], dev["vd"], dev["cd"])
+    ref = K.looped_ffn(*args, L=3)
+    kl.pin_weights_l2([dev["vg"], dev["vu"], dev["vd"]])
+    pinned = K.looped_ffn(*args, L=3)
+    kl.unpin_weights_l2()
+    torch.ops.titan.pin_weights_l2([dev["vg"], dev["vu"], dev["vd"]])
+    pinned2 = K.looped_ffn(*args, L=3)
+    torch.ops.titan.unpin_weights_l2()
+    torch.cuda.synchronize()
+    assert torch.equal(pinned, ref) and torch.equal(pinned2, ref)
+    assert K.read_status() == 0
