@@ -197,6 +197,7 @@ def main():
     ap.add_argument("--shared-gate-up", action="store_true")
     ap.add_argument("--layout", default="in_out", choices=["in_out", "out_in"], help="weight tile layout")
     ap.add_argument("--tokens", type=int, default=0, help="override T (profiling on a smaller case)")
+    ap.add_argument("--tile", type=int, default=0, help="override the tile size B (16, 32, 64, 128)")
     ap.add_argument("--ref-tokens", type=int, default=2048)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
@@ -213,14 +214,18 @@ def main():
                     help="keep the gate/up weight tiles in a persisting-L2 window (bell_pin_l2) while timing")
     ap.add_argument("--nccl-max-ctas", type=int, default=None,
                     help="N>1: NCCL CTA cap (default: the SM reserve)")
-    ap.add_argument("--direction", default="fwd", choices=["fwd", "bwd", "convert"],
-                    help="time the forward, the backward, or the dense -> Block-ELL conversion of the gate weight")
+    ap.add_argument("--direction", default="fwd", choices=["fwd", "fwd_train", "bwd", "convert"],
+                    help="time the forward, the training forward (with the gate/up intermediates the backward "
+                         "needs), the backward, or the dense -> Block-ELL conversion of the gate weight")
     args = ap.parse_args()
     from looped_blockell.synth import CONFIGS
     cfg = CONFIGS[args.config]
     if args.tokens:
         import dataclasses
         cfg = dataclasses.replace(cfg, T=args.tokens, name=f"{cfg.name}_T{args.tokens}")
+    if args.tile:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, B=args.tile, name=f"{cfg.name}_B{args.tile}")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
@@ -510,9 +515,10 @@ def run_gpu(args, cfg, rank, world):
     else:
         out = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
         h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
+        train = args.direction == "fwd_train"  # also write gate_pre and up_out, as the training forward does
 
         def step(x):
-            return ops._swiglu(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], True, lay, False,
+            return ops._swiglu(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], True, lay, train,
                                out=out, h=h, shared_topology=args.shared_gate_up)[0]
 
     x = c["x"]
@@ -658,12 +664,14 @@ def run_gpu(args, cfg, rank, world):
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC + (" (training forward, with gate/up intermediates)" if args.direction == "fwd_train"
+                                else ""),
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8 (ternary weights)" if cfg.dtype == "ternary" else "bf16",
             "data": "synthetic",
-            "config": {"workload": cfg.name, "T": T, "d_model": d, "d_ff": F, "B": cfg.B, "density": cfg.density,
-                       "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
+            "config": {"workload": cfg.name, "direction": args.direction, "T": T, "d_model": d, "d_ff": F,
+                       "B": cfg.B, "density": cfg.density, "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
                        "parallelism": f"dff{world}" if world > 1 else "single",
                        "L": cfg.L, "l2": l2_note + ("; gate/up tiles in a persisting-L2 window" if pinned is not None
                                                      else ""),

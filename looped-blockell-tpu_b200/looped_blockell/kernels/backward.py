@@ -108,19 +108,41 @@ def transposed_topology(mats: Sequence[torch.Tensor], C_blocks: int) -> Tuple[to
     return cols_t, tile_idx
 
 
+# (ids of the value and column tensors, C_blocks) -> (weak refs, versions, values_t):
+# the gathered tiles of a transposed weight, reused while the same tensors
+# keep the same contents (the optimizer bumps the version of what it updates)
+_TILE_CACHE: "OrderedDict[tuple, tuple]" = OrderedDict()
+_TILE_CACHE_MAX = 8
+
+
 def transpose_ell(values: Sequence[torch.Tensor], cols: Sequence[torch.Tensor], C_blocks: int,
                   layout: int = TILE_IN_OUT) -> Tuple[torch.Tensor, torch.Tensor, int]:
     """Transposed Block-ELL of the row-stacked weights ``values[i]``/``cols[i]``.
 
     Returns ``(values_t [C_blocks, K_t, B, B], cols_t [C_blocks, K_t], layout_t)``.
     The tiles are the same bytes, gathered; ``layout_t`` is the other tile
-    layout, which reads each tile as its transpose.
+    layout, which reads each tile as its transpose.  Both the topology and
+    the gathered tiles are cached per (tensor, version), so a backward over
+    unchanged weights gathers nothing.
     """
     cols_t, tile_idx = transposed_topology(cols, C_blocks)
+    lay_t = TILE_OUT_IN if layout == TILE_IN_OUT else TILE_IN_OUT
+    mats = list(values) + list(cols)
+    key = (C_blocks,) + tuple(id(m) for m in mats)
+    hit = _TILE_CACHE.get(key)
+    if hit is not None:
+        refs, versions, values_t = hit
+        if all(r() is m for r, m in zip(refs, mats)) and versions == tuple(m._version for m in mats):
+            _TILE_CACHE.move_to_end(key)
+            return values_t, cols_t, lay_t
+        del _TILE_CACHE[key]
     B = values[0].shape[-1]
     flat = torch.cat([v.reshape(-1, B, B) for v in values]) if len(values) > 1 else values[0].reshape(-1, B, B)
     values_t = flat.index_select(0, tile_idx.reshape(-1)).view(cols_t.shape[0], cols_t.shape[1], B, B)
-    return values_t, cols_t, (TILE_OUT_IN if layout == TILE_IN_OUT else TILE_IN_OUT)
+    _TILE_CACHE[key] = (tuple(weakref.ref(m) for m in mats), tuple(m._version for m in mats), values_t)
+    while len(_TILE_CACHE) > _TILE_CACHE_MAX:
+        _TILE_CACHE.popitem(last=False)
+    return values_t, cols_t, lay_t
 
 
 def silu_mul_bwd(d_h: torch.Tensor, gate_pre: torch.Tensor, up_out: torch.Tensor,

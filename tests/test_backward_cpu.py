@@ -98,3 +98,20 @@ def test_topology_cache_never_matches_a_different_tensor():
     c = torch.tensor([[1, 1], [1, 1]], dtype=torch.int32)
     tc, _ = K.transposed_topology([c], 2)
     assert tc.tolist() == [[-1, -1, -1, -1], [0, 0, 1, 1]]
+
+
+def test_transpose_ell_caches_tiles_per_weight_version():
+    """transpose_ell reuses its gathered tiles while the value and column
+    tensors keep their contents, and regathers after an in-place update."""
+    import torch
+    from looped_blockell.kernels.backward import transpose_ell
+    g = torch.Generator().manual_seed(0)
+    v = torch.randn(4, 2, 16, 16, generator=g)
+    c = torch.tensor([[0, 2], [1, 2], [0, 1], [2, -1]], dtype=torch.int32)
+    a = transpose_ell([v], [c], 3)
+    b = transpose_ell([v], [c], 3)
+    assert a[0] is b[0]
+    v.mul_(2.0)  # an optimizer-style in-place update bumps the version
+    d = transpose_ell([v], [c], 3)
+    assert d[0] is not a[0]
+    assert torch.equal(d[0], a[0] * 2.0)
