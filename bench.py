@@ -513,8 +513,9 @@ def run_gpu(args, cfg, rank, world):
             return looped_ffn(x, gain, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], L=cfg.L, layout=lay,
                               mode=mode)
     else:
-        out = torch.empty((T, d), dtype=torch.bfloat16, device="cuda")
-        h = torch.empty((T, F), dtype=torch.bfloat16, device="cuda")
+        act = c["x"].dtype  # bf16, or fp32 for the fp32 configuration
+        out = torch.empty((T, d), dtype=act, device="cuda")
+        h = torch.empty((T, F), dtype=act, device="cuda")
         train = args.direction == "fwd_train"  # also write gate_pre and up_out, as the training forward does
 
         def step(x):

@@ -36,7 +36,7 @@ from typing import Optional, Sequence, Tuple
 import torch
 
 from . import _lib
-from .ops import TILE_IN_OUT, TILE_OUT_IN, _check_cuda, _ell, _stream, block_ell_linear, plan_bytes
+from .ops import TILE_IN_OUT, TILE_OUT_IN, _check_cuda, _check_out, _ell, _stream, block_ell_linear, plan_bytes
 
 # (C_blocks, ids of the column-index tensors) -> (weak references, versions, result).
 # A hit needs the very same tensor objects (alive) at the same version: a new
@@ -158,6 +158,8 @@ def silu_mul_bwd(d_h: torch.Tensor, gate_pre: torch.Tensor, up_out: torch.Tensor
     T, F = d_h.shape
     if out is None:
         out = torch.empty((T, 2 * F), dtype=torch.bfloat16, device=d_h.device)
+    else:
+        _check_out("out", out, (T, 2 * F), torch.bfloat16, d_h.device)
     d_h, gate_pre, up_out = d_h.contiguous(), gate_pre.contiguous(), up_out.contiguous()
     with torch.cuda.device(d_h.device):
         _lib.check(_lib.load().bell_silu_mul_bwd_bf16(T, F, d_h.data_ptr(), gate_pre.data_ptr(), up_out.data_ptr(),
@@ -177,6 +179,8 @@ def down_silu_bwd(grad_out: torch.Tensor, v_down_t: torch.Tensor, ci_down_t: tor
         raise RuntimeError("grad_out must be [N, C*B] and gate_pre/up_out [N, d_ff]")
     if out is None:
         out = torch.empty((T, 2 * F), dtype=torch.bfloat16, device=grad_out.device)
+    else:
+        _check_out("out", out, (T, 2 * F), torch.bfloat16, grad_out.device)
     if T == 0:
         return out
     gate_pre, up_out = gate_pre.contiguous(), up_out.contiguous()

@@ -58,6 +58,15 @@ def _prep_ell(name, values, cols, dtype):
     return values.contiguous(), cols.contiguous()
 
 
+def _check_out(name: str, t: torch.Tensor, shape, dtype, device) -> None:
+    """A caller-supplied output or workspace must be exactly what the kernel
+    writes: the library trusts the pointer, so a smaller or differently typed
+    buffer would be written past its end."""
+    if tuple(t.shape) != tuple(shape) or t.dtype != dtype or t.device != device or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous {dtype} tensor of shape {tuple(shape)} on {device}; "
+                           f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+
+
 def plan_bytes(R_gu: int, K_g: int, K_u: int, R_d: int, K_d: int) -> int:
     return int(_lib.load().bell_plan_bytes(R_gu, K_g, K_u, R_d, K_d))
 
@@ -86,8 +95,14 @@ def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layo
     dev = x.device
     if h is None:
         h = torch.empty((N, d_ff), dtype=dtype, device=dev)
+    else:
+        _check_out("h", h, (N, d_ff), dtype, dev)
     if out is None:
         out = torch.empty((N, d_model), dtype=dtype, device=dev)
+    else:
+        _check_out("out", out, (N, d_model), dtype, dev)
+    if residual is not None:
+        _check_out("residual", residual, (N, d_model), dtype, dev)
     gate_pre = torch.empty((N, d_ff), dtype=dtype, device=dev) if want_intermediates else None
     up_out = torch.empty((N, d_ff), dtype=dtype, device=dev) if want_intermediates else None
     plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
@@ -128,6 +143,8 @@ def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: 
     d_ff = vg.shape[0] * B
     if h is None:
         h = torch.empty((N, d_ff), dtype=torch.bfloat16, device=x.device)
+    else:
+        _check_out("h", h, (N, d_ff), torch.bfloat16, x.device)
     plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
                        dtype=torch.uint8, device=x.device)
     desc = _lib.BellFFNDesc()
@@ -187,6 +204,8 @@ def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, 
         raise RuntimeError("fp32 inputs produce fp32 output")
     if out is None:
         out = torch.empty((N, R * B), dtype=out_dtype, device=x.device)
+    else:
+        _check_out("out", out, (N, R * B), out_dtype, x.device)
     if residual is not None:
         _check_cuda("residual", residual)
         if residual.shape != (N, R * B) or residual.dtype != dtype:

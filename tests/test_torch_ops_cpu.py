@@ -42,3 +42,19 @@ def test_titan_ops_have_no_cpu_kernel():
                                              z(4, 1, dtype=torch.int32), z(4, 1, 64, 64, dtype=torch.bfloat16),
                                              z(4, 1, dtype=torch.int32), z(2, 2, 64, 64, dtype=torch.bfloat16),
                                              z(2, 2, dtype=torch.int32), False)
+
+
+def test_caller_buffers_are_checked_before_the_library_sees_them():
+    """A caller-supplied output or workspace of the wrong size or dtype is
+    refused on the host (the library writes through the pointer as given)."""
+    import pytest
+    import torch
+    from looped_blockell.kernels import ops
+    good = torch.zeros(4, 8)
+    ops._check_out("out", good, (4, 8), torch.float32, good.device)
+    with pytest.raises(RuntimeError, match="must be a contiguous"):
+        ops._check_out("out", torch.zeros(4, 8, dtype=torch.bfloat16), (4, 8), torch.float32, good.device)
+    with pytest.raises(RuntimeError, match="must be a contiguous"):
+        ops._check_out("h", torch.zeros(4, 4), (4, 8), torch.float32, good.device)
+    with pytest.raises(RuntimeError, match="must be a contiguous"):
+        ops._check_out("h", torch.zeros(8, 4).t(), (4, 8), torch.float32, good.device)
