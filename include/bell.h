@@ -191,8 +191,9 @@ typedef struct BellTernaryEll {
 /*
  * Ternary SwiGLU forward.  x: [T, d_model] bf16.  Activations are quantised
  * per token to int8 by absmax (bitlinear.py:58-69, Qb = 128, clamp 127);
- * tile products accumulate exactly in int32 (tcgen05 kind::i8), are scaled
- * per tile in fp32 in ascending slot order, and divided by the token scale;
+ * tile products accumulate exactly in int32 (tcgen05 kind::i8), are combined
+ * per tile as acc = fma(scale, float(sum), acc) in fp32 in ascending slot
+ * order, and divided by the token scale;
  * h = silu(gate) * up in fp32 is re-quantised per token over all of d_ff for
  * the down projection.  out: [T, d_model] fp32 (+ x when add_residual).
  * Workspaces (caller-owned): q_x int8 [T, d_model], s_x f32 [T],

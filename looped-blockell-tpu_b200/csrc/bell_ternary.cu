@@ -7,13 +7,14 @@
 //
 // Pipeline of one forward:
 //   1. quantise x per token            -> q_x int8, s_x = 128 / absmax
-//   2. gate/up kernel: I_k = q_x . t_k (int32, TMEM), acc += s_k * I_k
+//   2. gate/up kernel: I_k = q_x . t_k (int32, TMEM), acc = fma(s_k, I_k, acc)
 //      (fp32, ascending k), gate = acc / s_x, h = silu(gate) * up (fp32),
 //      per-token |h| max via atomicMax
 //   3. quantise h with that max         -> q_h int8, s_h
 //   4. down kernel: same tile products on q_h, out = acc / s_h (+ x)
 // Arithmetic that must match the CPU oracle bit for bit uses explicit
-// round-to-nearest intrinsics (no FMA contraction).
+// round-to-nearest operations: one fused multiply-add per tile, otherwise no
+// contraction.
 #include <string>
 
 #include "bell_host.h"
@@ -160,31 +161,31 @@ __device__ __forceinline__ float2 f2_unpack(uint64_t v) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
   return r;
 }
-__device__ __forceinline__ uint64_t f2_add_rn(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 __device__ __forceinline__ uint64_t f2_sub_rn(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 
-// acc[j] += s * float(I[2j .. 2j+1]) for 8 pairs, exactly rounded: the int32
-// tile sums (|I| < 2^22) become floats through the 2^23 + 2^22 bias trick
-// (paired subtract), the products are scalar round-to-nearest multiplies and
-// the sums paired adds.  A paired multiply feeding a paired add measured as
-// fused (one rounding) on sm_100 even with .rn, so the multiply stays scalar
-// (mul.rn is never contracted).
+__device__ __forceinline__ uint64_t f2_fma_rn(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// acc[j] = fma(s, float(I[2j .. 2j+1]), acc[j]) for 8 pairs: the int32 tile
+// sums (|I| < 2^22) become exact floats through the 2^23 + 2^22 bias trick
+// (integer add, paired subtract), then one paired fused multiply-add, rounded
+// once, per pair of columns.
 __device__ __forceinline__ void scale_add16(uint64_t (&acc)[8], const uint32_t (&v)[16], float s) {
   const uint64_t bias2 = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t s2 = f2_pack(s, s);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float2 fi = f2_unpack(f2_sub_rn(f2_pack(__int_as_float(int(v[2 * j]) + 0x4B400000),
-                                                  __int_as_float(int(v[2 * j + 1]) + 0x4B400000)),
-                                          bias2));
-    acc[j] = f2_add_rn(acc[j], f2_pack(__fmul_rn(s, fi.x), __fmul_rn(s, fi.y)));
+    const uint64_t fi = f2_sub_rn(f2_pack(__int_as_float(int(v[2 * j]) + 0x4B400000),
+                                          __int_as_float(int(v[2 * j + 1]) + 0x4B400000)),
+                                  bias2);
+    acc[j] = f2_fma_rn(s2, fi, acc[j]);
   }
 }
 

@@ -31,7 +31,7 @@ __all__ = [
     "compact_block_ell", "dff_permutation", "block_ell_matmul", "block_ell_matmul_t", "silu", "swiglu_ffn", "swiglu_ffn_backward",
     "swiglu_ffn_backward_sparse", "rmsnorm", "looped_ffn",
     "ternary_quantize_tiles", "activation_quantize_int", "pack_ternary",
-    "unpack_ternary", "ternary_block_ell_matmul", "ternary_swiglu_ffn",
+    "unpack_ternary", "fma_f32", "ternary_block_ell_matmul", "ternary_swiglu_ffn",
     "bf16_round", "rel_l2", "nnz_flops",
 ]
 
@@ -414,15 +414,39 @@ def unpack_ternary(packed: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(np.swapaxes(kt, -1, -2))
 
 
+def fma_f32(a, b, c) -> np.ndarray:
+    """Correctly rounded float32 fused multiply-add ``fl(a*b + c)`` (what
+    ``fma.rn.f32`` computes), for float32 inputs, exactly.
+
+    a*b is exact in float64 (24 + 24 bits <= 53).  The float64 sum s = a*b + c
+    is made round-to-odd: when TwoSum shows it inexact and its last bit is
+    even, it moves one ulp toward the exact value.  Rounding a round-to-odd
+    value of at least 2*24 + 2 bits to float32 (nearest-even) gives the
+    correctly rounded result (Boldo & Melquiond, "Emulation of FMA and
+    correctly rounded sums: proved algorithms using rounding to odd", 2008).
+    """
+    a = np.asarray(a, dtype=np.float32).astype(np.float64)
+    b = np.asarray(b, dtype=np.float32).astype(np.float64)
+    c = np.asarray(c, dtype=np.float32).astype(np.float64)
+    p = a * b
+    s = p + c
+    bb = s - p
+    e = (p - (s - bb)) + (c - bb)  # TwoSum: s + e == p + c exactly
+    odd = (s.view(np.int64) & 1) == 1
+    fix = (e != 0) & ~odd
+    s = np.where(fix, np.nextafter(s, s + e), s)
+    return s.astype(np.float32)
+
+
 def ternary_block_ell_matmul(q: np.ndarray, scale: np.ndarray, t: np.ndarray,
                              s_w: np.ndarray, cols: np.ndarray, return_tile_sums=False):
     """Ternary Block-ELL matmul with exact integer tile sums.
 
     ``I_k[t, j] = sum_i q[t, c*B + i] * t[r, k, i, j]`` in int32 (exact), then
-    ``acc = fl(acc + fl(s_w[r,k] * float(I_k)))`` over the live k in ascending
-    order, all float32 round-to-nearest, and ``y = fl(acc / scale[t])``.
-    Dequantisation follows bonsai-test/bitlinear.py:34-69 (x ~ q / scale,
-    w ~ t * s); the tile-scale grouping is the packed format's.
+    ``acc = fma(s_w[r,k], float(I_k), acc)`` (float32, one rounding per tile)
+    over the live k in ascending order, and ``y = fl(acc / scale[t])``, all
+    round-to-nearest.  Dequantisation follows bonsai-test/bitlinear.py:34-69
+    (x ~ q / scale, w ~ t * s); the tile-scale grouping is the packed format's.
     """
     R, K, B, _ = t.shape
     T = q.shape[0]
@@ -440,8 +464,7 @@ def ternary_block_ell_matmul(q: np.ndarray, scale: np.ndarray, t: np.ndarray,
             I = np.rint(qf[:, c * B:(c + 1) * B] @ t[r, k].astype(np.float64)).astype(np.int32)
             if sums is not None:
                 sums[(r, k)] = I
-            prod = (np.float32(s_w[r, k]) * I.astype(np.float32)).astype(np.float32)
-            acc = (acc + prod).astype(np.float32)
+            acc = fma_f32(np.float32(s_w[r, k]), I.astype(np.float32), acc)
         y[:, r * B:(r + 1) * B] = (acc / scale[:, None].astype(np.float32)).astype(np.float32)
     if return_tile_sums:
         return y, sums

@@ -171,3 +171,30 @@ def test_oracle_sparse_backward_matches_dense(layout):
     sparse = O.swiglu_ffn_backward_sparse(x, *mats, dy, g, u, h)
     for a, b in zip(dense, sparse):
         np.testing.assert_allclose(a, b, rtol=1e-10, atol=1e-10)
+
+
+def test_fma_f32_is_correctly_rounded():
+    """The oracle's float32 FMA against exact rational arithmetic, on random
+    operands shaped like the ternary combination (scale x integer tile sum +
+    accumulator) and on cases built to land on a float32 rounding midpoint."""
+    from fractions import Fraction
+    rng = np.random.default_rng(7)
+    a = (np.abs(rng.standard_normal(4000)) * 0.02 + 1e-4).astype(np.float32)
+    b = rng.integers(-8192, 8193, size=4000).astype(np.float32)
+    c = (rng.standard_normal(4000) * 50).astype(np.float32)
+    # midpoints: c = -a*b rounded, plus half an ulp of a product-sized value
+    c[:500] = (-(a[:500].astype(np.float64) * b[:500])).astype(np.float32)
+    got = O.fma_f32(a, b, c)
+
+    def exact(ai, bi, ci):
+        v = Fraction(float(ai)) * Fraction(float(bi)) + Fraction(float(ci))
+        # nearest float32, ties to even, from the exact rational
+        f = np.float32(float(v))
+        lo, hi = sorted((f, np.nextafter(f, np.float32(np.inf) if Fraction(float(f)) < v else np.float32(-np.inf))))
+        dlo, dhi = abs(Fraction(float(lo)) - v), abs(Fraction(float(hi)) - v)
+        if dlo != dhi:
+            return lo if dlo < dhi else hi
+        return lo if (lo.view(np.int32) & 1) == 0 else hi
+
+    want = np.array([exact(x, y, z) for x, y, z in zip(a, b, c)], dtype=np.float32)
+    np.testing.assert_array_equal(got.view(np.int32), want.view(np.int32))
