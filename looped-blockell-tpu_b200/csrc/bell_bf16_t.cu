@@ -85,6 +85,13 @@ __global__ void __launch_bounds__(kThr, 1)
     bell_bf16_fmajor_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w0,
                             const __grid_constant__ CUtensorMap tm_w1, const Bf16Params p) {
   using C = FCfg<GU, SPLIT>;
+  // Split gate/up: the plan lists every gate step before the up steps, so the
+  // gate accumulator (TMEM columns [0, 256)) is handed to the epilogue
+  // (acc_full[0]) as soon as the last gate step is issued, and released by it
+  // (acc_empty[0]) before the up accumulator is done (acc_full[1] /
+  // acc_empty[1]).  The next unit's gate MMAs then start without waiting for
+  // this unit's epilogue to read the up columns.
+  constexpr bool STAG = GU && SPLIT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* id_tile = smem + C::NS * C::STAGE;  // linear only (ID_BYTES)
@@ -235,10 +242,20 @@ __global__ void __launch_bounds__(kThr, 1)
         const int n = p.counts[r] & 0xFFFF;
         const uint32_t* plan = p.plan + size_t(r) * p.S;
         uint32_t init0 = 0, init1 = 0;
+        bool up_ready = !STAG;  // staggered: the up columns are waited for at the first up step
         for (int s = 0; s < n && alive; ++s) {
           const uint32_t e = plan[s];
           const bool has0 = ((e >> 16) & 0xFFu) != kNone;
           const bool has1 = GU && (e >> 24) != kNone;
+          if (STAG && has1 && !up_ready) {  // every gate step is in: hand the gate columns over
+            mma_commit(&acc_full[0]);
+            if (!mbar_wait(&acc_empty[1], (uint32_t(i) & 1u) ^ 1u, ctl)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+            up_ready = true;
+          }
           for (int kc = 0; kc < B / kBK; ++kc) {
             if (!mbar_wait(&full[stage], phase, ctl)) {
               alive = false;
@@ -287,7 +304,12 @@ __global__ void __launch_bounds__(kThr, 1)
           }
         }
         if (!alive) break;
-        mma_commit(&acc_full[buf]);
+        if (STAG && !up_ready) {  // a unit without up steps
+          mma_commit(&acc_full[0]);
+          if (!mbar_wait(&acc_empty[1], (uint32_t(i) & 1u) ^ 1u, ctl)) break;
+          tc_fence_after();
+        }
+        mma_commit(&acc_full[STAG ? 1 : buf]);
       }
       if (!alive && issued_any) {
         mma_commit(drain);
@@ -314,7 +336,66 @@ __global__ void __launch_bounds__(kThr, 1)
       const int64_t feat = int64_t(r) * B + q * 32 + lane;
       const int64_t tok0 = int64_t(m) * TN + half * 128;
       const uint32_t lane_base = uint32_t(q * 32) << 16;
-      if constexpr (GU) {
+      if constexpr (STAG) {
+        // gate columns (already complete): SiLU(gate) of this feature's 128
+        // tokens as bf16 pairs, then the columns go back to the issuer
+        uint32_t hp[64];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t g[16];
+          tmem_ld16_sync(tmem + lane_base + uint32_t(half * 128 + j * 16), g);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float g0 = any0 ? __uint_as_float(g[2 * t]) : 0.f, g1 = any0 ? __uint_as_float(g[2 * t + 1]) : 0.f;
+            hp[j * 8 + t] = pack_bf16x2(silu_fast(g0), silu_fast(g1));
+          }
+          if (p.gate_pre) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const int64_t tok = tok0 + j * 16 + t;
+              if (tok < p.T)
+                static_cast<__nv_bfloat16*>(p.gate_pre)[tok * p.ld_out + feat] =
+                    __float2bfloat16(any0 ? __uint_as_float(g[t]) : 0.f);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[0]);
+        // up columns: h = SiLU(gate) * up, in place over the pairs
+        if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[1], uint32_t(i) & 1u, ctl))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // 16 columns at a time: the 64 pairs stay live throughout
+          uint32_t v[16];
+          tmem_ld16_sync(tmem + lane_base + uint32_t(256 + half * 128 + j * 16), v);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float u0 = any1 ? __uint_as_float(v[2 * t]) : 0.f, u1 = any1 ? __uint_as_float(v[2 * t + 1]) : 0.f;
+            const float2 sg = unpack_bf16x2(hp[j * 8 + t]);
+            hp[j * 8 + t] = pack_bf16x2(sg.x * u0, sg.y * u1);
+          }
+          if (p.up_out) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const int64_t tok = tok0 + j * 16 + t;
+              if (tok < p.T)
+                static_cast<__nv_bfloat16*>(p.up_out)[tok * p.ld_out + feat] =
+                    __float2bfloat16(any1 ? __uint_as_float(v[t]) : 0.f);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[1]);  // TMEM free: stores below overlap the next unit
+        __nv_bfloat16* hbase = static_cast<__nv_bfloat16*>(p.out) + feat;
+#pragma unroll
+        for (int t = 0; t < 64; ++t) {
+          const int64_t tok = tok0 + 2 * t;
+          if (tok < p.T) st_global_b16(hbase + tok * p.ld_out, uint16_t(hp[t] & 0xFFFFu));
+          if (tok + 1 < p.T) st_global_b16(hbase + (tok + 1) * p.ld_out, uint16_t(hp[t] >> 16));
+        }
+      } else if constexpr (GU) {
         uint32_t hp[64];  // 128 tokens of this feature, bf16 pairs
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
