@@ -207,7 +207,7 @@ def main():
     ap.add_argument("--check-rows", type=int, default=256, help="token rows per rank in the parity check")
     ap.add_argument("--sm-reserve", type=int, default=None,
                     help="N>1: SMs kept out of the GEMM grids for NCCL (default BELL_SM_RESERVE or 16)")
-    ap.add_argument("--chunks", type=int, default=4, help="N>1: token chunks of the reduce-scatter pipeline")
+    ap.add_argument("--chunks", type=int, default=8, help="N>1: token chunks of the reduce-scatter pipeline")
     ap.add_argument("--loop-mode", default="auto", choices=["auto", "launches", "persistent"],
                     help="config 4: the loop implementation")
     ap.add_argument("--l2-pin", action="store_true",
@@ -453,7 +453,7 @@ def run_gpu(args, cfg, rank, world):
     sm_reserve = None
     if world > 1:
         from looped_blockell.dist import default_sm_reserve, nccl_options
-        sm_reserve = default_sm_reserve() if args.sm_reserve is None else args.sm_reserve
+        sm_reserve = default_sm_reserve(world) if args.sm_reserve is None else args.sm_reserve
         nmax = args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local),
                                 pg_options=nccl_options(max_ctas=nmax or None))

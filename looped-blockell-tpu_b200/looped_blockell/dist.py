@@ -83,9 +83,15 @@ def nccl_options(max_ctas: Optional[int] = None, high_priority: bool = True):
     return opts
 
 
-def default_sm_reserve() -> int:
-    """SMs kept out of the GEMM grids while collectives run (BELL_SM_RESERVE)."""
-    return int(os.environ.get("BELL_SM_RESERVE", "16"))
+def default_sm_reserve(world: int = 2) -> int:
+    """SMs kept out of the GEMM grids while collectives run (BELL_SM_RESERVE
+    overrides).  Measured at config 5 on B200s: 16 was best at 2 ranks (of 0 /
+    16), 24 at 8 ranks (of 0 / 16 / 24 / 32), where each rank sends 7/8 of its
+    partial instead of 1/2."""
+    env = os.environ.get("BELL_SM_RESERVE")
+    if env is not None:
+        return int(env)
+    return 16 if world <= 2 else 24
 
 
 def pick_chunks(T: int, world: int, want: int = 4) -> int:
@@ -98,7 +104,7 @@ def pick_chunks(T: int, world: int, want: int = 4) -> int:
 class ShardedSwiGLU:
     """This rank's share of a d_ff-split SwiGLU forward (bf16)."""
 
-    def __init__(self, vg, cg, vu, cu, vd, cd, rank: int, world: int, chunks: int = 4, group=None,
+    def __init__(self, vg, cg, vu, cu, vd, cd, rank: int, world: int, chunks: int = 8, group=None,
                  sm_reserve: Optional[int] = None):
         R_f = vg.shape[0]
         self.B = vg.shape[2]
@@ -109,7 +115,7 @@ class ShardedSwiGLU:
         self.vd, self.cd = repack_down(vd, cd, self.lo, self.hi)
         self.d_model = vd.shape[0] * self.B
         self.want_chunks = chunks
-        self.sm_reserve = default_sm_reserve() if sm_reserve is None else int(sm_reserve)
+        self.sm_reserve = default_sm_reserve(world) if sm_reserve is None else int(sm_reserve)
         self._bufs = {}
 
     def grid_cap(self, dev) -> int:
