@@ -208,6 +208,9 @@ def main():
     ap.add_argument("--sm-reserve", type=int, default=None,
                     help="N>1: SMs kept out of the GEMM grids for NCCL (default BELL_SM_RESERVE or 16)")
     ap.add_argument("--chunks", type=int, default=8, help="N>1: token chunks of the reduce-scatter pipeline")
+    ap.add_argument("--exchange", choices=["nccl", "copy"], default=None,
+                    help="N>1: sum the partials with an NCCL reduce-scatter or with copy engines + an owner-side "
+                         "sum kernel (default: looped_blockell.dist.default_exchange)")
     ap.add_argument("--loop-mode", default="auto", choices=["auto", "launches", "persistent"],
                     help="config 4: the loop implementation")
     ap.add_argument("--l2-pin", action="store_true",
@@ -452,8 +455,9 @@ def run_gpu(args, cfg, rank, world):
     torch.cuda.set_device(local)
     sm_reserve = None
     if world > 1:
-        from looped_blockell.dist import default_sm_reserve, nccl_options
-        sm_reserve = default_sm_reserve(world) if args.sm_reserve is None else args.sm_reserve
+        from looped_blockell.dist import default_exchange, default_sm_reserve, nccl_options
+        exchange = args.exchange or default_exchange()
+        sm_reserve = default_sm_reserve(world, exchange) if args.sm_reserve is None else args.sm_reserve
         nmax = args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local),
                                 pg_options=nccl_options(max_ctas=nmax or None))
@@ -476,7 +480,7 @@ def run_gpu(args, cfg, rank, world):
     if world > 1:
         from looped_blockell.dist import ShardedSwiGLU
         model = ShardedSwiGLU(c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], rank, world, chunks=args.chunks,
-                              sm_reserve=sm_reserve)
+                              sm_reserve=sm_reserve, exchange=exchange)
         step_out = model.alloc_out(T, c["x"])
         launches_per_step = model.launches_per_step(T)
 
@@ -676,7 +680,7 @@ def run_gpu(args, cfg, rank, world):
                        "parallelism": f"dff{world}" if world > 1 else "single",
                        "L": cfg.L, "l2": l2_note + ("; gate/up tiles in a persisting-L2 window" if pinned is not None
                                                      else ""),
-                       **({"chunks": args.chunks, "sm_reserve": sm_reserve,
+                       **({"chunks": args.chunks, "sm_reserve": sm_reserve, "exchange": model.exchange,
                            "nccl_max_ctas": args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve}
                           if world > 1 else {})},
             "tflops_effective": tflops, "tflops_effective_per_gpu": tflops / world,

@@ -391,6 +391,34 @@ typedef struct BellDenseToEllDesc {
 
 int bell_dense_to_ell(const BellDenseToEllDesc* desc, void* stream);
 
+/* --------------------------------------------------- sharded exchange */
+
+/* Owner-side sum of the d_ff-sharded forward (no reference counterpart: the
+ * reference has no multi-GPU path).  out[r, c] = bf16(fp32 sum over slices
+ * s = 0 .. n_slices-1 in ascending order, then + residual[r, c] when residual
+ * is non-NULL), rounded once.  Slice s, row r is at slices + s * slice_stride
+ * + r * ld_slice, except slice local_slot (-1: none), read from local + r *
+ * ld_local.  All bf16; d % 8 == 0; pointers 16-byte aligned; strides in
+ * elements, multiples of 8.  max_ctas > 0 caps the grid (the SMs that
+ * concurrent GEMM launches leave free). */
+int bell_sum_slices_bf16(const void* slices, int64_t slice_stride, int64_t ld_slice, int32_t n_slices,
+                         int32_t local_slot, const void* local, int64_t ld_local, const void* residual,
+                         int64_t ld_res, void* out, int64_t ld_out, int64_t rows, int32_t d, int32_t max_ctas,
+                         void* stream);
+/* One stream-ordered copy of `bytes` between two device addresses (a peer
+ * GPU's memory mapped into this process included: copy engines over NVLink). */
+int bell_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);
+/* Enable direct access from the current device to `peer` (already enabled is
+ * success); without it a copy between them is staged through the host. */
+int bell_enable_peer_access(int32_t peer);
+/* CUDA IPC for the sharded exchange's inboxes: the 64-byte handle of the
+ * allocation holding `ptr` and ptr's offset in it; mapping such a handle of
+ * another process into the current device's address space (peer access
+ * enabled as needed; *ptr_out = mapped base + offset); unmapping a base. */
+int bell_ipc_handle(const void* ptr, void* handle_out, uint64_t* offset_out);
+int bell_ipc_open(const void* handle, uint64_t offset, void** ptr_out, void** base_out);
+int bell_ipc_close(void* base);
+
 /* ---------------------------------------------------------------- L2 pins */
 
 /* Persisting-L2 window over [base, base+bytes) on `stream`; replaces

@@ -29,6 +29,7 @@ scaling plan asks for.
 
 from __future__ import annotations
 
+import ctypes as C
 import os
 from typing import List, Optional, Tuple
 
@@ -83,15 +84,45 @@ def nccl_options(max_ctas: Optional[int] = None, high_priority: bool = True):
     return opts
 
 
-def default_sm_reserve(world: int = 2) -> int:
+def default_sm_reserve(world: int = 2, exchange: str = "nccl") -> int:
     """SMs kept out of the GEMM grids while collectives run (BELL_SM_RESERVE
-    overrides).  Measured at config 5 on B200s: 16 was best at 2 ranks (of 0 /
-    16), 24 at 8 ranks (of 0 / 16 / 24 / 32), where each rank sends 7/8 of its
-    partial instead of 1/2."""
+    overrides).  NCCL reduce-scatter, measured at config 5 on B200s: 16 was
+    best at 2 ranks (of 0 / 16), 24 at 8 ranks (of 0 / 16 / 24 / 32), where
+    each rank sends 7/8 of its partial instead of 1/2.  The copy exchange
+    moves data on the copy engines and only needs room for its barrier's
+    one-CTA all-reduce."""
     env = os.environ.get("BELL_SM_RESERVE")
     if env is not None:
         return int(env)
+    if exchange == "copy":
+        return 4
     return 16 if world <= 2 else 24
+
+
+_IPC_MAPPED = {}  # (device, allocation handle) -> base of its mapping in this process
+
+
+def _ipc_map(handle: bytes, dev) -> int:
+    """Base address in this process of another process's allocation, mapped
+    into ``dev``'s context once (a second inbox in the same allocation reuses
+    the mapping)."""
+    key = (dev.index, handle)
+    base = _IPC_MAPPED.get(key)
+    if base is None:
+        from .kernels import _lib
+        p, b = C.c_void_p(), C.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().bell_ipc_open((C.c_uint8 * 64).from_buffer_copy(handle), 0, C.byref(p),
+                                                 C.byref(b)), "ShardedSwiGLU inbox")
+        base = int(b.value)
+        _IPC_MAPPED[key] = base
+    return base
+
+
+def default_exchange() -> str:
+    """How the sharded forward sums the partials: ``"nccl"`` (reduce-scatter)
+    or ``"copy"`` (copy engines + owner-side sum).  BELL_EXCHANGE overrides."""
+    return os.environ.get("BELL_EXCHANGE", "nccl")
 
 
 def pick_chunks(T: int, world: int, want: int = 4) -> int:
@@ -105,7 +136,7 @@ class ShardedSwiGLU:
     """This rank's share of a d_ff-split SwiGLU forward (bf16)."""
 
     def __init__(self, vg, cg, vu, cu, vd, cd, rank: int, world: int, chunks: int = 8, group=None,
-                 sm_reserve: Optional[int] = None):
+                 sm_reserve: Optional[int] = None, exchange: Optional[str] = None):
         R_f = vg.shape[0]
         self.B = vg.shape[2]
         self.rank, self.world, self.group = rank, world, group
@@ -115,7 +146,10 @@ class ShardedSwiGLU:
         self.vd, self.cd = repack_down(vd, cd, self.lo, self.hi)
         self.d_model = vd.shape[0] * self.B
         self.want_chunks = chunks
-        self.sm_reserve = default_sm_reserve(world) if sm_reserve is None else int(sm_reserve)
+        self.exchange = default_exchange() if exchange is None else exchange
+        if self.exchange not in ("nccl", "copy"):
+            raise ValueError(f"ShardedSwiGLU: exchange must be 'nccl' or 'copy', not {self.exchange!r}")
+        self.sm_reserve = default_sm_reserve(world, self.exchange) if sm_reserve is None else int(sm_reserve)
         self._bufs = {}
 
     def grid_cap(self, dev) -> int:
@@ -136,8 +170,10 @@ class ShardedSwiGLU:
         return n, T // n, T // n // self.world
 
     def launches_per_step(self, T: int) -> int:
-        # per chunk: plan + gate/up, plan + down (the NCCL reduce-scatter is not counted)
-        return 4 * pick_chunks(T, self.world, self.want_chunks)
+        # per chunk: plan + gate/up, plan + down, and with the copy exchange the owner-side sum
+        # (NCCL's kernels and the copies are not counted)
+        per_chunk = 5 if self.exchange == "copy" and self.world > 1 else 4
+        return per_chunk * pick_chunks(T, self.world, self.want_chunks)
 
     def alloc_out(self, T: int, x: torch.Tensor) -> torch.Tensor:
         return torch.empty((T // self.world, self.d_model), dtype=torch.bfloat16, device=x.device)
@@ -151,6 +187,8 @@ class ShardedSwiGLU:
 
     def forward(self, x: torch.Tensor, out: torch.Tensor = None, add_residual: bool = True) -> torch.Tensor:
         """This rank's token slice of the full forward (bf16, CUDA)."""
+        if self.exchange == "copy" and self.world > 1:
+            return self.forward_copy(x, out, add_residual)
         from .kernels.ops import block_ell_gate_up, block_ell_linear
         T = x.shape[0]
         _, Tc, per = self._chunking(T)
@@ -166,6 +204,113 @@ class ShardedSwiGLU:
                              residual_rows=own if fold else None, max_ctas=cap)
 
         return self.run_chunks(x, partial_fn, out, add_residual=add_residual and not fold)
+
+    def _inbox(self, per: int, dev):
+        """This rank's inbox ``[2, N, per, d_model]`` bf16 (chunk parity, source
+        rank, row, column) and the address of every rank's inbox in this
+        process: CUDA IPC handles are exchanged once through the process group
+        and mapped into this rank's own device context (``bell_ipc_open``), so
+        copies into a peer's inbox run device to device over NVLink."""
+        key = ("inbox", per, dev.index)
+        got = self._bufs.get(key)
+        if got is None:
+            import torch.distributed as dist
+            from .kernels import _lib
+            lib = _lib.load()
+            box = torch.empty((2, self.world, per, self.d_model), dtype=torch.bfloat16, device=dev)
+            h, off = (C.c_uint8 * 64)(), C.c_uint64(0)
+            with torch.cuda.device(dev):
+                _lib.check(lib.bell_ipc_handle(C.c_void_p(box.data_ptr()), h, C.byref(off)), "ShardedSwiGLU inbox")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, (bytes(h), int(off.value)), group=self.group)
+            ptrs = []
+            for r, (hb, o) in enumerate(handles):
+                ptrs.append(box.data_ptr() if r == self.rank else _ipc_map(hb, dev) + o)
+            got = (box, ptrs)
+            self._bufs[key] = got
+        return got
+
+    def forward_copy(self, x: torch.Tensor, out: torch.Tensor = None, add_residual: bool = True) -> torch.Tensor:
+        """``forward`` with the exchange on the copy engines instead of an NCCL
+        reduce-scatter.  For chunk i (partials and inbox halves alternate):
+
+        * compute stream: gate/up(i), then the owner-side sum of chunk i-2,
+          then down(i) into this rank's partial [Tc, d] (all tokens of the
+          chunk, this rank's d_ff share);
+        * copy stream: one ``cudaMemcpyAsync`` per peer moves the peer's rows
+          of partial(i) into the peer's inbox slot for this rank (ranks send in
+          rotation, r -> r+1, r+2, ..., so each inbox takes one stream at a
+          time); one chunk later a one-element all-reduce (barrier i) marks
+          that every rank's copies of chunk i have landed and every rank's sum
+          of chunk i-1 is done, so chunk i+1 may refill that inbox half;
+        * the sum (``bell_sum_slices_bf16``, every SM) adds the N slices, this
+          rank's own from its partial, and the residual, in rank order.
+
+        Lagging the sum two chunks behind lets each chunk's copies run beside
+        the next chunk and a half of GEMMs; the GEMMs leave only ``sm_reserve``
+        SMs for the barrier's NCCL kernel."""
+        import torch.distributed as dist
+        from .kernels import _lib
+        from .kernels.ops import block_ell_gate_up, block_ell_linear, sum_slices
+        T = x.shape[0]
+        n, Tc, per = self._chunking(T)
+        dev = x.device
+        d = self.d_model
+        if out is None:
+            out = torch.empty((T // self.world, d), dtype=torch.bfloat16, device=dev)
+        box, peers = self._inbox(per, dev)
+        slot_bytes = per * d * 2  # one (half, source) slot of an inbox
+        h = self._buf("h", (Tc, (self.hi - self.lo) * self.B), torch.bfloat16, dev)
+        partial = [self._buf(f"p{i}", (Tc, d), torch.bfloat16, dev) for i in range(2)]
+        flag = self._buf("flag", (1,), torch.float32, dev)
+        cap = self.grid_cap(dev)
+        lib = _lib.load()
+        cur = torch.cuda.current_stream(dev)
+        s_cp = self._stream("copy", dev)
+        s_cp.wait_stream(cur)  # the inbox and partials' previous users are done
+        ev = {k: [torch.cuda.Event() for _ in range(n)] for k in ("down", "bar", "sum")}
+        order = [(self.rank + k) % self.world for k in range(1, self.world)]
+        me = slice(self.rank * per, (self.rank + 1) * per)
+
+        def enq_sum(j):  # compute stream
+            cur.wait_event(ev["bar"][j])
+            xj = x[j * Tc:(j + 1) * Tc]
+            sum_slices(box[j % 2], out[j * per:(j + 1) * per], local=partial[j % 2][me], local_slot=self.rank,
+                       residual=xj[me] if add_residual else None)
+            ev["sum"][j].record(cur)
+
+        def enq_barrier(j):  # copy stream: copies(j) landed everywhere, sum(j-1) done everywhere
+            with torch.cuda.stream(s_cp):
+                if j >= 1:
+                    s_cp.wait_event(ev["sum"][j - 1])
+                dist.all_reduce(flag, group=self.group)
+                ev["bar"][j].record(s_cp)
+
+        st = C.c_void_p(s_cp.cuda_stream)
+        for i in range(n):
+            P = partial[i % 2]
+            block_ell_gate_up(x[i * Tc:(i + 1) * Tc], self.vg, self.cg, self.vu, self.cu, self.vd, self.cd, h=h,
+                              max_ctas=cap)
+            if i >= 2:
+                enq_sum(i - 2)  # also the last reader of P before down(i) overwrites it
+            if i >= 1:
+                enq_barrier(i - 1)
+            block_ell_linear(h, self.vd, self.cd, out=P, max_ctas=cap)
+            ev["down"][i].record(cur)
+            s_cp.wait_event(ev["down"][i])
+            for o in order:  # after barrier i-1: every rank's sum of chunk i-2 has read this inbox half
+                dst = peers[o] + ((i % 2) * self.world + self.rank) * slot_bytes
+                _lib.check(lib.bell_memcpy_async(C.c_void_p(dst), C.c_void_p(P[o * per:(o + 1) * per].data_ptr()),
+                                                 slot_bytes, st), "forward_copy")
+        if n >= 2:
+            enq_sum(n - 2)
+        enq_barrier(n - 1)
+        enq_sum(n - 1)
+        with torch.cuda.stream(s_cp):  # every rank's sums are done before any rank refills an inbox
+            s_cp.wait_event(ev["sum"][n - 1])
+            dist.all_reduce(flag, group=self.group)
+        cur.wait_stream(s_cp)
+        return out
 
     def _can_fold(self, per: int) -> bool:
         """Whether the down kernel can add the residual to this rank's rows: at

@@ -124,6 +124,14 @@ SIGNATURES = {
     "bell_sddmm_bf16": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
     "bell_sddmm_f32": (C.c_int, [C.POINTER(BellSddmmDesc), C.c_void_p]),
     "bell_dense_to_ell": (C.c_int, [C.POINTER(BellDenseToEllDesc), C.c_void_p]),
+    "bell_sum_slices_bf16": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                       C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int64, C.c_int32,
+                                       C.c_int32, C.c_void_p]),
+    "bell_memcpy_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "bell_enable_peer_access": (C.c_int, [C.c_int32]),
+    "bell_ipc_handle": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_uint64)]),
+    "bell_ipc_open": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    "bell_ipc_close": (C.c_int, [C.c_void_p]),
     "bell_pin_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "bell_unpin_l2": (C.c_int, [C.c_void_p]),
 }

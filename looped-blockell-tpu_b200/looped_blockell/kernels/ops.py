@@ -257,6 +257,34 @@ def rmsnorm(x: torch.Tensor, gain: torch.Tensor, eps: float = 1e-5) -> torch.Ten
     return out
 
 
+def sum_slices(slices: torch.Tensor, out: torch.Tensor, local: Optional[torch.Tensor] = None, local_slot: int = -1,
+               residual: Optional[torch.Tensor] = None, max_ctas: int = 0) -> torch.Tensor:
+    """``out = bf16(sum_s slices[s] (+ residual))`` in fp32, ascending s, one
+    rounding (``bell_sum_slices_bf16``).  ``slices`` is ``[n, rows, d]`` bf16
+    (rows contiguous, slices any stride); slice ``local_slot`` is taken from
+    ``local`` ``[rows, d]`` instead (``slices[local_slot]`` is not read)."""
+    _check_cuda("slices", slices)
+    if slices.dim() != 3 or slices.dtype != torch.bfloat16 or slices.stride(2) != 1:
+        raise RuntimeError("sum_slices: slices must be [n, rows, d] bf16 with contiguous rows")
+    n, rows, d = slices.shape
+    for name, t in (("out", out), ("local", local), ("residual", residual)):
+        if t is None:
+            continue
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or tuple(t.shape) != (rows, d) or t.stride(1) != 1:
+            raise RuntimeError(f"sum_slices: {name} must be [{rows}, {d}] bf16 with contiguous rows")
+        if t.device != slices.device:
+            raise RuntimeError(f"sum_slices: {name} is on {t.device}, slices on {slices.device}")
+    if (local is None) != (local_slot < 0):
+        raise RuntimeError("sum_slices: give local together with local_slot >= 0")
+    with torch.cuda.device(slices.device):
+        _lib.check(_lib.load().bell_sum_slices_bf16(
+            slices.data_ptr(), slices.stride(0), slices.stride(1), n, local_slot, _ptr(local),
+            local.stride(0) if local is not None else 0, _ptr(residual),
+            residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), rows, d,
+            int(max_ctas), _stream()), "sum_slices")
+    return out
+
+
 def read_status(clear: bool = True) -> int:
     """Read (and clear) the library's device status word (synchronises)."""
     v = C.c_int32(0)

@@ -1,8 +1,10 @@
 """torchrun worker for tests/test_gpu_multi.py: the d_ff-sharded forward on N
-GPUs (NCCL reduce-scatter).  Every rank checks a sample of the token rows it
-owns against the CPU oracle (fp64 on the same bf16 inputs, rel-L2 <= 1e-2),
-through the device-buffer forward, and checks that the token-sliced
-host-buffer forward gives the same bits.  Exit code 0 = pass."""
+GPUs, with the NCCL reduce-scatter and with the copy-engine exchange.  Every
+rank checks a sample of the token rows it owns against the CPU oracle (fp64
+on the same bf16 inputs, rel-L2 <= 1e-2) through the device-buffer forward
+of each exchange, checks that the token-sliced host-buffer forward gives the
+NCCL forward's bits, and that a second copy-exchange call (reused inboxes)
+repeats the first bit for bit.  Exit code 0 = pass."""
 
 import datetime
 import os
@@ -43,6 +45,15 @@ def main():
         err = O.rel_l2(got, ref)
         print(f"rank {rank}/{world} {cfg.name}: rel-L2 vs oracle on {pick.size} owned rows {err:.3e}", flush=True)
         ok &= err < 1e-2
+        # copy-engine exchange: same rows, owner-side sum in rank order
+        mc = ShardedSwiGLU(c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], rank, world, exchange="copy")
+        outs = [mc.forward(c["x"]) for _ in range(2)]
+        torch.cuda.synchronize()
+        err_c = O.rel_l2(f(outs[0].index_select(0, torch.from_numpy(pick).cuda())), ref)
+        rep = torch.equal(outs[0], outs[1])
+        print(f"rank {rank}/{world} {cfg.name}: copy exchange rel-L2 vs oracle {err_c:.3e}, "
+              f"second call bit-identical: {rep}", flush=True)
+        ok &= err_c < 1e-2 and rep
         # host-buffer entry: this rank's token rows in, the same rows of the result out
         x_own = c["x"].index_select(0, rows.cuda()).cpu().pin_memory()
         for _ in range(2):  # twice: the second call reuses the cached buffers and streams
