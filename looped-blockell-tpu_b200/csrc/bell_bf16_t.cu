@@ -337,6 +337,16 @@ __global__ void __launch_bounds__(kThr, 1)
       const int64_t tok0 = int64_t(m) * TN + half * 128;
       const uint32_t lane_base = uint32_t(q * 32) << 16;
       if constexpr (STAG) {
+        // 16 tokens of this lane's feature into an optional [T, ld_out] output: the
+        // address steps by one row per token, and a tile wholly inside T skips the checks
+        const bool whole = tok0 + 128 <= p.T;
+        auto store16 = [&](void* dst, int64_t tok_start, const uint32_t (&v)[16], bool live) {
+          __nv_bfloat16* ptr = static_cast<__nv_bfloat16*>(dst) + tok_start * p.ld_out + feat;
+#pragma unroll
+          for (int t = 0; t < 16; ++t, ptr += p.ld_out)
+            if (whole || tok_start + t < p.T)
+              st_global_b16(ptr, __bfloat16_as_ushort(__float2bfloat16(live ? __uint_as_float(v[t]) : 0.f)));
+        };
         // gate columns (already complete): SiLU(gate) of this feature's 128
         // tokens as bf16 pairs, then the columns go back to the issuer
         uint32_t hp[64];
@@ -349,15 +359,7 @@ __global__ void __launch_bounds__(kThr, 1)
             const float g0 = any0 ? __uint_as_float(g[2 * t]) : 0.f, g1 = any0 ? __uint_as_float(g[2 * t + 1]) : 0.f;
             hp[j * 8 + t] = pack_bf16x2(silu_fast(g0), silu_fast(g1));
           }
-          if (p.gate_pre) {
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const int64_t tok = tok0 + j * 16 + t;
-              if (tok < p.T)
-                static_cast<__nv_bfloat16*>(p.gate_pre)[tok * p.ld_out + feat] =
-                    __float2bfloat16(any0 ? __uint_as_float(g[t]) : 0.f);
-            }
-          }
+          if (p.gate_pre) store16(p.gate_pre, tok0 + j * 16, g, any0);
         }
         tc_fence_before();
         __syncwarp();
@@ -375,25 +377,16 @@ __global__ void __launch_bounds__(kThr, 1)
             const float2 sg = unpack_bf16x2(hp[j * 8 + t]);
             hp[j * 8 + t] = pack_bf16x2(sg.x * u0, sg.y * u1);
           }
-          if (p.up_out) {
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const int64_t tok = tok0 + j * 16 + t;
-              if (tok < p.T)
-                static_cast<__nv_bfloat16*>(p.up_out)[tok * p.ld_out + feat] =
-                    __float2bfloat16(any1 ? __uint_as_float(v[t]) : 0.f);
-            }
-          }
+          if (p.up_out) store16(p.up_out, tok0 + j * 16, v, any1);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[1]);  // TMEM free: stores below overlap the next unit
-        __nv_bfloat16* hbase = static_cast<__nv_bfloat16*>(p.out) + feat;
+        __nv_bfloat16* hptr = static_cast<__nv_bfloat16*>(p.out) + tok0 * p.ld_out + feat;
 #pragma unroll
-        for (int t = 0; t < 64; ++t) {
-          const int64_t tok = tok0 + 2 * t;
-          if (tok < p.T) st_global_b16(hbase + tok * p.ld_out, uint16_t(hp[t] & 0xFFFFu));
-          if (tok + 1 < p.T) st_global_b16(hbase + (tok + 1) * p.ld_out, uint16_t(hp[t] >> 16));
+        for (int t = 0; t < 64; ++t, hptr += 2 * p.ld_out) {
+          if (whole || tok0 + 2 * t < p.T) st_global_b16(hptr, uint16_t(hp[t] & 0xFFFFu));
+          if (whole || tok0 + 2 * t + 1 < p.T) st_global_b16(hptr + p.ld_out, uint16_t(hp[t] >> 16));
         }
       } else if constexpr (GU) {
         uint32_t hp[64];  // 128 tokens of this feature, bf16 pairs
