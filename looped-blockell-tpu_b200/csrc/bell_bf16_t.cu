@@ -336,10 +336,11 @@ __global__ void __launch_bounds__(kThr, 1)
       const int64_t feat = int64_t(r) * B + q * 32 + lane;
       const int64_t tok0 = int64_t(m) * TN + half * 128;
       const uint32_t lane_base = uint32_t(q * 32) << 16;
+      // gate/up outputs are written token by token down this lane's feature column: the address
+      // steps one row per token, and a half tile wholly inside T skips the bounds checks (the
+      // linear epilogue keeps per-element indexing, measured faster for the down projection)
+      const bool whole = tok0 + 128 <= p.T;
       if constexpr (STAG) {
-        // 16 tokens of this lane's feature into an optional [T, ld_out] output: the
-        // address steps by one row per token, and a tile wholly inside T skips the checks
-        const bool whole = tok0 + 128 <= p.T;
         auto store16 = [&](void* dst, int64_t tok_start, const uint32_t (&v)[16], bool live) {
           __nv_bfloat16* ptr = static_cast<__nv_bfloat16*>(dst) + tok_start * p.ld_out + feat;
 #pragma unroll
@@ -401,27 +402,28 @@ __global__ void __launch_bounds__(kThr, 1)
             const float u0 = any1 ? __uint_as_float(v[2 * t]) : 0.f, u1 = any1 ? __uint_as_float(v[2 * t + 1]) : 0.f;
             hp[j * 16 + t] = pack_bf16x2(silu_fast(g0) * u0, silu_fast(g1) * u1);
           }
-          if (p.gate_pre || p.up_out) {  // optional intermediates, token by token
+          if (p.gate_pre || p.up_out) {  // optional intermediates, one row pointer step per token
+            const int64_t tj = tok0 + j * 32;
+            const int64_t o0 = tj * p.ld_out + feat;
+            __nv_bfloat16* gptr = static_cast<__nv_bfloat16*>(p.gate_pre) + o0;
+            __nv_bfloat16* uptr = static_cast<__nv_bfloat16*>(p.up_out) + o0;
 #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              const int64_t tok = tok0 + j * 32 + t;
-              if (tok >= p.T) continue;
-              const int64_t off = tok * p.ld_out + feat;
+            for (int t = 0; t < 32; ++t, gptr += p.ld_out, uptr += p.ld_out) {
+              if (!whole && tj + t >= p.T) continue;
               const float gv = any0 ? __uint_as_float(g[t]) : 0.f, uv = any1 ? __uint_as_float(v[t]) : 0.f;
-              if (p.gate_pre) static_cast<__nv_bfloat16*>(p.gate_pre)[off] = __float2bfloat16(gv);
-              if (p.up_out) static_cast<__nv_bfloat16*>(p.up_out)[off] = __float2bfloat16(uv);
+              if (p.gate_pre) st_global_b16(gptr, __bfloat16_as_ushort(__float2bfloat16(gv)));
+              if (p.up_out) st_global_b16(uptr, __bfloat16_as_ushort(__float2bfloat16(uv)));
             }
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);  // TMEM free: stores below overlap the next unit
-        __nv_bfloat16* hbase = static_cast<__nv_bfloat16*>(p.out) + feat;
+        __nv_bfloat16* hptr = static_cast<__nv_bfloat16*>(p.out) + tok0 * p.ld_out + feat;
 #pragma unroll
-        for (int t = 0; t < 64; ++t) {
-          const int64_t tok = tok0 + 2 * t;
-          if (tok < p.T) st_global_b16(hbase + tok * p.ld_out, uint16_t(hp[t] & 0xFFFFu));
-          if (tok + 1 < p.T) st_global_b16(hbase + (tok + 1) * p.ld_out, uint16_t(hp[t] >> 16));
+        for (int t = 0; t < 64; ++t, hptr += 2 * p.ld_out) {
+          if (whole || tok0 + 2 * t < p.T) st_global_b16(hptr, uint16_t(hp[t] & 0xFFFFu));
+          if (whole || tok0 + 2 * t + 1 < p.T) st_global_b16(hptr + p.ld_out, uint16_t(hp[t] >> 16));
         }
       } else {
 #pragma unroll 1
