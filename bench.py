@@ -93,7 +93,7 @@ class ClockSampler:
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate/up launch, from ncu captures
 # of the same command on a B200.  Config 5 is captured at T=32768 (x 256 MiB) and scaled by the
 # units of a full launch (x8): the kernel walks the same unit order, so traffic grows in proportion.
-GU_DRAM_BYTES = {(5, 262144): 8 * (1.831003e9 + 1.057941e9), (2, 32768): 1.42730e8 + 4.82981e8}
+GU_DRAM_BYTES = {(5, 262144): 8 * (2.390204e9 + 1.065839e9), (2, 32768): 1.42730e8 + 4.82981e8}
 GU_DRAM_NOTE = {5: "ncu dram__bytes_{read,write}.sum at T=32768, scaled x8 by units",
                 2: "ncu dram__bytes_{read,write}.sum on the full config-2 launch"}
 
