@@ -119,6 +119,18 @@ def _ipc_map(handle: bytes, dev) -> int:
     return base
 
 
+def close_ipc_mappings() -> None:
+    """Unmap every peer inbox this process mapped for the copy exchange.  Call
+    it after the last ``forward`` of every ``ShardedSwiGLU`` that used
+    ``exchange="copy"`` (the mappings otherwise live until the process ends)."""
+    from .kernels import _lib
+    lib = _lib.load() if _IPC_MAPPED else None
+    for (dev_index, _), base in list(_IPC_MAPPED.items()):
+        with torch.cuda.device(dev_index):
+            _lib.check(lib.bell_ipc_close(C.c_void_p(base)), "close_ipc_mappings")
+    _IPC_MAPPED.clear()
+
+
 def default_exchange() -> str:
     """How the sharded forward sums the partials: ``"nccl"`` (reduce-scatter)
     or ``"copy"`` (copy engines + owner-side sum).  BELL_EXCHANGE overrides."""

@@ -64,6 +64,10 @@ def main():
     t = torch.tensor([0 if ok else 1], device="cuda")
     dist.all_reduce(t)
     dist.barrier()
+    from looped_blockell.dist import close_ipc_mappings
+    torch.cuda.synchronize()
+    close_ipc_mappings()
+    dist.barrier()
     dist.destroy_process_group()
     sys.exit(int(t.item() != 0))
 

@@ -167,3 +167,46 @@ def test_uneven_token_count_is_refused(T):
         model.forward(torch.zeros((T, C * B), dtype=torch.bfloat16))
     with pytest.raises(ValueError, match="cannot be split evenly"):
         model._chunking(T)
+
+
+def _tiny_model(**kw):
+    from looped_blockell.dist import ShardedSwiGLU
+    rng = np.random.default_rng(1)
+    R, C, K, B = 4, 2, 2, 64
+    v = torch.from_numpy(rng.standard_normal((R, K, B, B)).astype(np.float32)).to(torch.bfloat16)
+    cols = torch.tensor([[0, 1]] * R, dtype=torch.int32)
+    vd = torch.from_numpy(rng.standard_normal((C, K, B, B)).astype(np.float32)).to(torch.bfloat16)
+    cd = torch.tensor([[0, 3], [1, 2]], dtype=torch.int32)
+    return ShardedSwiGLU(v, cols, v, cols, vd, cd, **kw)
+
+
+def test_exchange_choice_and_defaults(monkeypatch):
+    """The exchange is validated; each exchange gets its own SM-reserve
+    default (the NCCL one grows with the rank count), and the environment
+    overrides both."""
+    from looped_blockell.dist import default_exchange, default_sm_reserve
+    monkeypatch.delenv("BELL_SM_RESERVE", raising=False)
+    monkeypatch.delenv("BELL_EXCHANGE", raising=False)
+    assert default_exchange() == "nccl"
+    assert default_sm_reserve(2) == 16 and default_sm_reserve(8) == 24
+    assert default_sm_reserve(8, "copy") == 4
+    assert _tiny_model(rank=0, world=8).sm_reserve == 24
+    assert _tiny_model(rank=0, world=8, exchange="copy").sm_reserve == 4
+    monkeypatch.setenv("BELL_EXCHANGE", "copy")
+    monkeypatch.setenv("BELL_SM_RESERVE", "12")
+    m = _tiny_model(rank=1, world=2)
+    assert m.exchange == "copy" and m.sm_reserve == 12
+    with pytest.raises(ValueError, match="exchange must be"):
+        _tiny_model(rank=0, world=2, exchange="ring")
+
+
+def test_launch_count_per_exchange():
+    """Per chunk: plan + gate/up and plan + down, plus the owner-side sum with
+    the copy exchange (NCCL's kernels and the copies are not this library's
+    launches); one rank runs no exchange at all."""
+    from looped_blockell.dist import pick_chunks
+    T = 8 * 4 * 256
+    n = pick_chunks(T, 4, 8)
+    assert _tiny_model(rank=0, world=4).launches_per_step(T) == 4 * n
+    assert _tiny_model(rank=0, world=4, exchange="copy").launches_per_step(T) == 5 * n
+    assert _tiny_model(rank=0, world=1, exchange="copy").launches_per_step(T) == 4 * pick_chunks(T, 1, 8)
