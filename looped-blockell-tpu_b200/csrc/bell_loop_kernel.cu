@@ -31,6 +31,7 @@
 // 4: 6.3 MB) stay L2-resident across all iterations.
 //
 // Tile size 64, either tile layout; other tile sizes use the launch loop.
+#include <cstdlib>
 #include <string>
 
 #include "bell_bf16.cuh"
@@ -43,6 +44,9 @@ namespace loopk {
 
 static constexpr int B = 64;
 using G = eng::Geo<B, true>;  // ring / accumulator geometry of both phases
+// Token tiles per wave.  Config 4 (64 tiles): 4 -> 2.23 ms, 8 -> 1.77 ms,
+// 16 -> 1.51 ms, 32 -> 1.48 ms; 16 keeps four waves per iteration.
+static constexpr int kWaveTiles = 16;
 
 struct LoopParams {
   int64_t T;
@@ -62,20 +66,41 @@ struct LoopParams {
 // With the producer, issuer and epilogue of both phases all inlined into one
 // kernel body, the down phase computed wrong results (while each phase alone
 // was exact); any one role kept out of line gives exact results, so all are.
+// A reference argument of a non-inlined function points into the caller's
+// stack frame (local memory), and the role loops store through generic
+// pointers that the compiler cannot tell apart from it, so every field read
+// would be a local-memory load inside the issue, copy and store loops.  Each
+// wrapper therefore copies its arguments into locals once per call (they stay
+// in registers) and writes the pipeline state back when the phase ends.
 template <bool GU, bool W_MN>
-__device__ __noinline__ bool loop_produce(const Bf16Params& p, const CUtensorMap* ta, const CUtensorMap* tw0,
-                                          const CUtensorMap* tw1, const eng::Smem& s, eng::ProdState& st, int i_base,
-                                          int pid, const Ctl& ctl, uint64_t pol_a, uint64_t pol_w) {
-  return eng::produce<B, GU, W_MN, G>(p, ta, tw0, tw1, s, st, i_base, pid, ctl, pol_a, pol_w);
+__device__ __noinline__ bool loop_produce(const Bf16Params& p_in, const CUtensorMap* ta, const CUtensorMap* tw0,
+                                          const CUtensorMap* tw1, const eng::Smem& s_in, eng::ProdState& st_io,
+                                          int i_base, int pid, const Ctl& ctl_in, uint64_t pol_a, uint64_t pol_w) {
+  const Bf16Params p = p_in;
+  const eng::Smem s = s_in;
+  const Ctl ctl = ctl_in;
+  eng::ProdState st = st_io;
+  const bool ok = eng::produce<B, GU, W_MN, G>(p, ta, tw0, tw1, s, st, i_base, pid, ctl, pol_a, pol_w);
+  st_io = st;
+  return ok;
 }
 template <bool GU, bool W_MN>
-__device__ __noinline__ bool loop_issue(const Bf16Params& p, const eng::Smem& s, uint32_t tmem, eng::IssueState& st,
-                                        int i_base, int k, bool leader, const Ctl& ctl) {
-  return eng::issue<B, GU, W_MN, G>(p, s, tmem, st, i_base, k, leader, ctl);
+__device__ __noinline__ bool loop_issue(const Bf16Params& p_in, const eng::Smem& s_in, uint32_t tmem,
+                                        eng::IssueState& st_io, int i_base, int k, bool leader, const Ctl& ctl_in) {
+  const Bf16Params p = p_in;
+  const eng::Smem s = s_in;
+  const Ctl ctl = ctl_in;
+  eng::IssueState st = st_io;
+  const bool ok = eng::issue<B, GU, W_MN, G>(p, s, tmem, st, i_base, k, leader, ctl);
+  st_io = st;
+  return ok;
 }
 template <bool GU>
-__device__ __noinline__ bool loop_epilogue(const Bf16Params& p, const eng::Smem& s, uint32_t tmem, int i_base,
-                                           const Ctl& ctl) {
+__device__ __noinline__ bool loop_epilogue(const Bf16Params& p_in, const eng::Smem& s_in, uint32_t tmem, int i_base,
+                                           const Ctl& ctl_in) {
+  const Bf16Params p = p_in;
+  const eng::Smem s = s_in;
+  const Ctl ctl = ctl_in;
   return eng::epilogue<B, GU, G>(p, s, tmem, i_base, ctl);
 }
 
@@ -217,8 +242,11 @@ int loop_persistent_bf16(const BellLoopDesc* d, const BellEll& g, const BellEll&
   p.cnt_gu = reinterpret_cast<unsigned*>(static_cast<char*>(d->workspace) + W.counters);
   p.cnt_dn = p.cnt_gu + n_mt;
   float* ss = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + W.ss);
-  // waves of 8 token tiles, at least two per iteration (see the kernel)
-  p.seg_tiles = n_mt >= 16 ? 8 : int32_t((n_mt + 1) / 2);
+  // waves of kWaveTiles token tiles, at least two waves per iteration (see
+  // the kernel); BELL_LOOP_WAVE_TILES overrides, read per call
+  const char* wave_env = std::getenv("BELL_LOOP_WAVE_TILES");
+  const int64_t want = wave_env && std::atoi(wave_env) > 0 ? std::atoi(wave_env) : kWaveTiles;
+  p.seg_tiles = n_mt >= 2 * want ? int32_t(want) : int32_t((n_mt + 1) / 2);
   p.n_seg = int32_t((n_mt + p.seg_tiles - 1) / p.seg_tiles);
   if (p.n_seg < 2) p.n_seg = 2;
   p.status = status;
