@@ -217,6 +217,8 @@ def main():
                     help="keep the gate/up weight tiles in a persisting-L2 window (bell_pin_l2) while timing")
     ap.add_argument("--nccl-max-ctas", type=int, default=None,
                     help="N>1: NCCL CTA cap (default: the SM reserve)")
+    ap.add_argument("--f32-method", default=None, choices=["auto", "simt", "bf16x6"],
+                    help="config 1 (fp32): FFMA on the CUDA cores or the bf16x6 split on the tensor cores")
     ap.add_argument("--direction", default="fwd", choices=["fwd", "fwd_train", "bwd", "convert"],
                     help="time the forward, the training forward (with the gate/up intermediates the backward "
                          "needs), the backward, or the dense -> Block-ELL conversion of the gate weight")
@@ -420,8 +422,8 @@ def run_convert(args, cfg, rank, world):
 def parity_check(cfg, c, lay, out, rows, n_rows: int, seed: int = 0):
     """rel-L2 of ``out`` (this rank's result rows; ``rows`` = their token
     indices) against the CPU oracle on a sample of ``n_rows`` of them,
-    computed from the same bf16 inputs the GPU saw.  Runs outside the timed
-    region."""
+    computed from the same (bf16 or fp32) inputs the GPU saw.  Runs outside
+    the timed region."""
     import numpy as np
     import torch
     import oracle as O
@@ -477,6 +479,7 @@ def run_gpu(args, cfg, rank, world):
         kl.pin_weights_l2([pinned])
     T, d, F = cfg.T, cfg.d_model, cfg.d_ff
     launches_per_step = 3
+    f32_method = None  # config 1: the fp32 method that runs
     if world > 1:
         from looped_blockell.dist import ShardedSwiGLU
         model = ShardedSwiGLU(c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], rank, world, chunks=args.chunks,
@@ -519,12 +522,17 @@ def run_gpu(args, cfg, rank, world):
     else:
         act = c["x"].dtype  # bf16, or fp32 for the fp32 configuration
         out = torch.empty((T, d), dtype=act, device="cuda")
-        h = torch.empty((T, F), dtype=act, device="cuda")
         train = args.direction == "fwd_train"  # also write gate_pre and up_out, as the training forward does
+        if act == torch.float32:
+            from looped_blockell.kernels import f32x
+            f32_method = f32x.resolve(args.f32_method, T, cfg.K_gu, cfg.K_gu, cfg.K_d)
+            launches_per_step = 8 if f32_method == "bf16x6" else 3  # split, 3 x (plan + linear), SiLU split
+        # the bf16x6 fp32 forward keeps h in bf16 parts inside its workspace
+        h = None if f32_method == "bf16x6" else torch.empty((T, F), dtype=act, device="cuda")
 
         def step(x):
             return ops._swiglu(x, c["vg"], c["cg"], c["vu"], c["cu"], c["vd"], c["cd"], True, lay, train,
-                               out=out, h=h, shared_topology=args.shared_gate_up)[0]
+                               out=out, h=h, shared_topology=args.shared_gate_up, fp32_method=f32_method)[0]
 
     x = c["x"]
     for _ in range(args.warmup):
@@ -570,7 +578,7 @@ def run_gpu(args, cfg, rank, world):
     # parity of one more (untimed) step's output against the CPU oracle: every
     # rank checks a sample of the token rows it holds; the worst rank is reported
     parity = None
-    if not args.no_check and cfg.dtype == "bf16":
+    if not args.no_check and cfg.dtype in ("bf16", "f32"):
         import torch as _t
         res = step(x)
         _t.cuda.synchronize()
@@ -584,8 +592,8 @@ def run_gpu(args, cfg, rank, world):
             t = _t.tensor([err], device="cuda", dtype=_t.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             err = float(t.item())
-        parity = {"rel_l2": err, "tolerance": 1e-2, "rows_per_rank": n_chk, "ranks": world,
-                  "oracle": "oracle/bell_oracle.py (fp64, on the bf16 inputs)"}
+        parity = {"rel_l2": err, "tolerance": 1e-5 if cfg.dtype == "f32" else 1e-2, "rows_per_rank": n_chk,
+                  "ranks": world, "oracle": f"oracle/bell_oracle.py (fp64, on the {cfg.dtype} inputs the GPU saw)"}
 
     # dominant kernel: the fused gate/up kernel, timed alone with events
     gu = None
@@ -673,13 +681,15 @@ def run_gpu(args, cfg, rank, world):
                                 else ""),
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8 (ternary weights)" if cfg.dtype == "ternary" else "bf16",
+            "vs_baseline": None,
+            "dtype": {"ternary": "int8 (ternary weights)", "f32": "f32"}.get(cfg.dtype, "bf16"),
             "data": "synthetic",
             "config": {"workload": cfg.name, "direction": args.direction, "T": T, "d_model": d, "d_ff": F,
                        "B": cfg.B, "density": cfg.density, "gate_up_topology": "shared" if args.shared_gate_up else "independent", "tile_layout": args.layout,
                        "parallelism": f"dff{world}" if world > 1 else "single",
                        "L": cfg.L, "l2": l2_note + ("; gate/up tiles in a persisting-L2 window" if pinned is not None
                                                      else ""),
+                       **({"f32_method": f32_method} if f32_method else {}),
                        **({"chunks": args.chunks, "sm_reserve": sm_reserve, "exchange": model.exchange,
                            "nccl_max_ctas": args.nccl_max_ctas if args.nccl_max_ctas is not None else sm_reserve}
                           if world > 1 else {})},

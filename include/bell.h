@@ -167,9 +167,43 @@ int bell_down_bf16(const BellFFNDesc* desc, void* stream);
  * (looped_blockell/layers/block_ell.py:149-182). */
 int bell_linear_bf16(const BellLinearDesc* desc, void* stream);
 
-/* fp32 SwiGLU forward (all tensors f32; accuracy target rel-L2 <= 1e-5). */
+/* fp32 SwiGLU forward (all tensors f32; accuracy target rel-L2 <= 1e-5).
+ * FFMA on the CUDA cores.  Replaces the fp32 evaluation of the reference's
+ * block_ell_matmul / MLPBlock (looped_blockell/layers/block_ell.py:149-182,
+ * mlp.py:119-145), which the reference runs in fp32 (config.py dtype). */
 int bell_swiglu_fwd_f32(const BellFFNDesc* desc, void* stream);
 int bell_linear_f32(const BellLinearDesc* desc, void* stream);
+
+/*
+ * The same fp32 forward on the bf16 tensor cores ("bf16x6": every fp32
+ * operand split into three bf16 parts, the six leading cross products
+ * accumulated in fp32; Henry, Tang & Heinecke, ARITH 2019).  Same semantics
+ * and accuracy target as bell_swiglu_fwd_f32 (block_ell.py:149-182,
+ * mlp.py:119-145).
+ *
+ * The weights are first expanded once by bell_f32x_expand_ell into bf16
+ * Block-ELL matrices over one activation matrix A = [h parts | x parts]
+ * ([T, 3 d_ff + 3 d_model] bf16, column blocks CA = 3 d_ff/B + 3 d_model/B):
+ *   gate, up: col_base = 3 d_ff/B, part_cols = d_model/B, ident_base = -1;
+ *   down:     col_base = 0, part_cols = d_ff/B, ident_base = 3 d_ff/B,
+ *             ident_stride = d_model/B (three identity slots per block-row
+ *             that add the residual inside the accumulator; ident_base = -1
+ *             leaves them out, and then add_residual must be 0).
+ * values6 holds [R, K6, B, B] bf16 and cols6 [R, K6] int32 with
+ * K6 = bell_f32x_slots(K, with_identity) = 6K (+3), at most 254.
+ *
+ * bell_swiglu_fwd_f32x takes a BellFFNDesc with dtype F32: x, residual
+ * (NULL -> x), out, and the optional h / gate_pre / up_out outputs are fp32;
+ * gate / up / down are the expanded matrices (C = CA, tile size B); desc->plan
+ * is unused.  `workspace` holds bell_f32x_workspace_bytes() bytes (256-byte
+ * aligned).  Stream-ordered; allocates nothing.
+ */
+int32_t bell_f32x_slots(int32_t K, int32_t with_identity);
+int bell_f32x_expand_ell(const BellEll* w_f32, int32_t col_base, int32_t part_cols, int32_t ident_base,
+                         int32_t ident_stride, void* values6, int32_t* cols6, void* stream);
+size_t bell_f32x_workspace_bytes(int64_t T, int32_t d_model, int32_t d_ff, int32_t B, int32_t K_gate6,
+                                 int32_t K_up6, int32_t K_down6);
+int bell_swiglu_fwd_f32x(const BellFFNDesc* desc, void* workspace, void* stream);
 
 /* ---------------------------------------------------------------- ternary */
 

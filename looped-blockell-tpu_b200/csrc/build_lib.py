@@ -21,7 +21,7 @@ INCLUDE = os.path.join(REPO, "include")
 BUILD = os.path.join(CSRC, "_build")
 LIB = os.path.join(PKG_ROOT, "looped_blockell", "libbell_b200.so")
 
-SOURCES = ["bell_common.cu", "bell_bf16.cu", "bell_bf16_t.cu", "bell_f32.cu", "bell_ternary.cu", "bell_loop.cu", "bell_loop_kernel.cu", "bell_noalloc.cu", "bell_bwd.cu", "bell_convert.cu", "bell_small.cu", "bell_exchange.cu"]
+SOURCES = ["bell_common.cu", "bell_bf16.cu", "bell_bf16_t.cu", "bell_f32.cu", "bell_ternary.cu", "bell_loop.cu", "bell_loop_kernel.cu", "bell_noalloc.cu", "bell_bwd.cu", "bell_convert.cu", "bell_small.cu", "bell_exchange.cu", "bell_f32x.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills", "-I" + INCLUDE, "-I" + CSRC]

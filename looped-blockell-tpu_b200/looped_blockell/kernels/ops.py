@@ -18,7 +18,7 @@ from typing import Optional, Sequence
 
 import torch
 
-from . import _lib
+from . import _lib, f32x
 
 TILE_IN_OUT = _lib.BELL_TILE_IN_OUT
 TILE_OUT_IN = _lib.BELL_TILE_OUT_IN
@@ -72,7 +72,10 @@ def plan_bytes(R_gu: int, K_g: int, K_u: int, R_d: int, K_d: int) -> int:
 
 
 def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, want_intermediates,
-            residual=None, out=None, h=None, shared_topology=False):
+            residual=None, out=None, h=None, shared_topology=False, fp32_method=None):
+    """The forward behind every SwiGLU op.  fp32 inputs run the method
+    ``f32x.resolve(fp32_method, ...)`` picks: FFMA on the CUDA cores or the
+    bf16x6 split on the tensor cores (same results within the fp32 target)."""
     lib = _lib.load()
     _check_cuda("x", x)
     if x.dim() != 2:
@@ -93,8 +96,10 @@ def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layo
     if d_model % B != 0:
         raise RuntimeError(f"d_model={d_model} is not a multiple of the tile size {B}")
     dev = x.device
+    split = dtype == torch.float32 and f32x.resolve(fp32_method, N, vg.shape[1], vu.shape[1], vd.shape[1]) == "bf16x6"
     if h is None:
-        h = torch.empty((N, d_ff), dtype=dtype, device=dev)
+        # the bf16x6 forward keeps h in bf16 parts; an fp32 copy only when asked for
+        h = torch.empty((N, d_ff), dtype=dtype, device=dev) if not split or want_intermediates else None
     else:
         _check_out("h", h, (N, d_ff), dtype, dev)
     if out is None:
@@ -105,6 +110,9 @@ def _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layo
         _check_out("residual", residual, (N, d_model), dtype, dev)
     gate_pre = torch.empty((N, d_ff), dtype=dtype, device=dev) if want_intermediates else None
     up_out = torch.empty((N, d_ff), dtype=dtype, device=dev) if want_intermediates else None
+    if split:
+        f32x.swiglu_fwd_f32x(x, vg, cg, vu, cu, vd, cd, add_residual, layout, out, h, gate_pre, up_out, residual)
+        return out, h, gate_pre, up_out
     plan = torch.empty(plan_bytes(vg.shape[0], vg.shape[1], vu.shape[1], vd.shape[0], vd.shape[1]),
                        dtype=torch.uint8, device=dev)
     desc = _lib.BellFFNDesc()
@@ -160,22 +168,24 @@ def block_ell_gate_up(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, layout: 
 
 
 def block_ell_swiglu_fwd(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual: bool = False,
-                         layout: int = TILE_IN_OUT, shared_topology: bool = False) -> torch.Tensor:
+                         layout: int = TILE_IN_OUT, shared_topology: bool = False,
+                         fp32_method: Optional[str] = None) -> torch.Tensor:
     """``W_down(silu(W_gate x) * W_up x) (+ x)`` — reference titan::block_ell_swiglu_fwd.
 
     ``shared_topology=True`` tells the kernel that gate and up hold the same
     column lists (the reference MLPBlock's default); results are identical
-    either way, only the schedule changes."""
+    either way, only the schedule changes.  ``fp32_method`` (fp32 inputs):
+    ``"auto"`` (default), ``"simt"`` or ``"bf16x6"`` (``kernels.f32x``)."""
     return _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, False,
-                   shared_topology=shared_topology)[0]
+                   shared_topology=shared_topology, fp32_method=fp32_method)[0]
 
 
 def block_ell_swiglu_fwd_with_intermediate(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down,
                                            add_residual: bool = False, layout: int = TILE_IN_OUT,
-                                           shared_topology: bool = False):
+                                           shared_topology: bool = False, fp32_method: Optional[str] = None):
     """Returns (result, h, gate_pre_act, up_output) like the reference op (block_ell_ops.cpp:65-76)."""
     return _swiglu(x, v_gate, ci_gate, v_up, ci_up, v_down, ci_down, add_residual, layout, True,
-                   shared_topology=shared_topology)
+                   shared_topology=shared_topology, fp32_method=fp32_method)
 
 
 def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, residual: Optional[torch.Tensor] = None,

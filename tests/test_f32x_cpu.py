@@ -1,0 +1,55 @@
+"""Host logic of the fp32 tensor-core forward (bf16x6 split), no GPU: which
+method a call runs, the expanded slot counts and the workspace size."""
+
+import os
+
+import pytest
+
+
+def _f32x():
+    from looped_blockell.kernels import f32x
+    return f32x
+
+
+def _lib():
+    from looped_blockell.kernels import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        pytest.skip("library not built")
+    return _lib.load()
+
+
+def test_method_choice():
+    f = _f32x()
+    assert f.resolve("simt", 1 << 20, 2, 2, 8) == "simt"
+    assert f.resolve("bf16x6", 1, 2, 2, 8) == "bf16x6"
+    assert f.resolve("auto", f.AUTO_MIN_TOKENS, 2, 2, 8) == "bf16x6"
+    assert f.resolve("auto", f.AUTO_MIN_TOKENS - 1, 2, 2, 8) == "simt"
+    # 6K slots per gate/up row and 6K + 3 per down row must fit in 254
+    assert f.resolve("auto", 1 << 16, 42, 42, 41) == "bf16x6"
+    assert f.resolve("auto", 1 << 16, 43, 2, 8) == "simt"
+    assert f.resolve("auto", 1 << 16, 2, 2, 42) == "simt"
+    with pytest.raises(RuntimeError):
+        f.resolve("bf16x6", 1 << 16, 2, 2, 42)
+    with pytest.raises(RuntimeError):
+        f.resolve("tf32", 1 << 16, 2, 2, 8)
+
+
+def test_method_env_override(monkeypatch):
+    f = _f32x()
+    monkeypatch.setenv("BELL_F32_METHOD", "simt")
+    assert f.resolve(None, 1 << 20, 2, 2, 8) == "simt"
+    monkeypatch.setenv("BELL_F32_METHOD", "bogus")
+    with pytest.raises(RuntimeError):
+        f.resolve(None, 1 << 20, 2, 2, 8)
+
+
+def test_slots_and_workspace_bytes():
+    lib = _lib()
+    assert lib.bell_f32x_slots(8, 0) == 48 and lib.bell_f32x_slots(8, 1) == 51
+    T, d, F, B = 1000, 512, 2048, 64
+    up = lambda v: (v + 255) // 256 * 256  # noqa: E731
+    plan = max(lib.bell_plan_bytes(0, 0, 0, F // B, 12), lib.bell_plan_bytes(0, 0, 0, d // B, 51))
+    want = up(T * (3 * F + 3 * d) * 2) + 2 * up(T * F * 4) + up(plan)
+    assert lib.bell_f32x_workspace_bytes(T, d, F, B, 12, 12, 51) == want
+    assert lib.bell_f32x_workspace_bytes(-1, d, F, B, 12, 12, 51) == 0
+    assert lib.bell_f32x_workspace_bytes(T, d, F, B, 0, 12, 51) == 0
