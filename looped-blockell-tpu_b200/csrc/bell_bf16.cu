@@ -35,6 +35,11 @@ __global__ void __launch_bounds__(eng::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const eng::Smem s = eng::carve<G>(smem_raw);
   const uint32_t tmem = eng::setup<G>(s);
+  // launched behind the previous kernel (programmatic dependent launch): the
+  // set-up above touched only this CTA's shared memory and TMEM; every global
+  // read and write comes after the predecessor has completed
+  griddep_wait();
+  griddep_launch();
   Ctl ctl{s.abort_flag, p.status, p.timeout_ns};
   const int warp = threadIdx.x >> 5;
   switch (eng::role_of(warp)) {
@@ -513,6 +518,25 @@ static int launch_bf16(const CUtensorMap& a, const CUtensorMap& w0, const CUtens
   if (int rc = device_sm_count(&sms)) return rc;
   const int64_t units = int64_t(p.n_mtiles) * p.R;
   if (units == 0) return BELL_OK;
+  if (p.pdl) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(grid_size(units, sms, p.max_ctas)));
+    cfg.blockDim = dim3(eng::kThreads);
+    cfg.dynamicSmemBytes = G::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, w0, w1, p);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(BELL_ERR_LAUNCH, std::string(GU ? "bell gate/up kernel: " : "bell linear kernel: ") +
+                                       cudaGetErrorString(e));
+    }
+    return BELL_OK;
+  }
   kern<<<grid_size(units, sms, p.max_ctas), eng::kThreads, G::SMEM_BYTES, stream>>>(a, w0, w1, p);
   return check_launch(GU ? "bell gate/up kernel" : "bell linear kernel");
 }
@@ -588,7 +612,7 @@ int check_ffn(const BellFFNDesc* d, int dtype) {
   return BELL_OK;
 }
 
-int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
+int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl) {
   const BellEll &g = d->gate, &u = d->up;
   const bool sm = g.B < 64;  // small tiles: bell_small.cu
   CUtensorMap ma, mg, mu;
@@ -622,10 +646,11 @@ int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.split = use_split(d) ? 1 : 0;  // must match the plan built by launch_ffn_plan
   p.max_ctas = d->max_ctas;
   if (sm) return launch_small(true, g.B, g.layout == BELL_TILE_IN_OUT, ma, mg, mu, p, s);
+  p.pdl = pdl ? 1 : 0;
   return dispatch_bf16<true>(g.B, g.layout, ma, mg, mu, p, s);
 }
 
-int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
+int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl) {
   const BellEll& w = d->down;
   const bool sm = w.B < 64;
   CUtensorMap ma, mw;
@@ -656,6 +681,7 @@ int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s) {
   p.max_ctas = d->max_ctas;
   p.status = status;
   p.timeout_ns = wait_budget_ns();
+  p.pdl = pdl ? 1 : 0;
   if (sm) return launch_small(false, w.B, w.layout == BELL_TILE_IN_OUT, ma, mw, mw, p, s);
   return dispatch_bf16<false>(w.B, w.layout, ma, mw, mw, p, s);
 }

@@ -67,6 +67,9 @@ struct Bf16Params {
   // segment of the unit sequence this launch (or loop-kernel phase) covers:
   // units [u_begin, u_end) of the n_mtiles * R (u_end == 0: all of them)
   int32_t u_begin, u_end;
+  // launch with programmatic stream serialization (the engine kernel waits for
+  // its predecessor after its shared-memory / TMEM set-up; tile 64/128 engine only)
+  int32_t pdl;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {

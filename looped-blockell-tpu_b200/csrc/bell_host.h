@@ -60,8 +60,10 @@ int launch_plan_ex(const int32_t* ci_g, int32_t K_g, const int32_t* ci_u, int32_
 // and the down (linear + residual) launch, on an already-built plan.
 int check_ffn(const BellFFNDesc* d, int dtype);
 int launch_ffn_plan(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
-int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
-int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
+// pdl: launch with programmatic stream serialization (honoured by the tile-64/
+// 128 token-major engine, which waits for its predecessor after its set-up).
+int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl = false);
+int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl = false);
 
 // Workspace of the loop: per-tile counters, per-row partial sums of squares
 // and the gain-scaled gate/up tiles (tile size 64; other sizes need none).

@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256) bell_rmsnorm_kernel(const __nv_bfloat16* 
                                                            const __nv_bfloat16* __restrict__ gain,
                                                            __nv_bfloat16* __restrict__ out, int64_t T, int d,
                                                            float eps) {
+  griddep_wait();  // launched behind the previous kernel of the loop: its writes first
   const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -244,9 +245,29 @@ LoopWs loop_ws(int64_t T, int32_t d_model, int32_t R_gu, int32_t K_g, int32_t K_
   return L;
 }
 
-int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d, float eps, cudaStream_t s) {
+int launch_rmsnorm(const void* x, const void* gain, void* out, int64_t T, int d, float eps, cudaStream_t s,
+                   bool pdl = false) {
   if (T == 0) return BELL_OK;
   const int64_t blocks = (T + 7) / 8;
+  if (pdl) {  // programmatic stream serialization: the kernel waits for its predecessor first
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(blocks));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, bell_rmsnorm_kernel, static_cast<const __nv_bfloat16*>(x),
+                                       static_cast<const __nv_bfloat16*>(gain), static_cast<__nv_bfloat16*>(out), T,
+                                       d, eps);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(BELL_ERR_LAUNCH, std::string("bell_rmsnorm_kernel: ") + cudaGetErrorString(e));
+    }
+    return BELL_OK;
+  }
   bell_rmsnorm_kernel<<<unsigned(blocks), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                         static_cast<const __nv_bfloat16*>(gain),
                                                         static_cast<__nv_bfloat16*>(out), T, d, eps);
@@ -365,11 +386,17 @@ int bell_loop_fwd_bf16(const BellLoopDesc* d, void* stream) {
   if (!status) return BELL_ERR_LAUNCH;
   if (int rc = launch_ffn_plan(&f, status, s)) return rc;
   if (!fold) {
+    // Each launch of the chain may start while its predecessor drains
+    // (programmatic dependent launch): its CTAs do their set-up, then wait for
+    // the predecessor's completion before touching global memory.
+    // BELL_LOOP_PDL=0 launches them plainly.
+    const char* pdl_env = std::getenv("BELL_LOOP_PDL");
+    const bool pdl = !(pdl_env && pdl_env[0] == '0');
     for (int it = 0; it < d->L; ++it) {
-      if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s)) return rc;
-      if (int rc = gate_up_bf16(&f, status, s)) return rc;
+      if (int rc = launch_rmsnorm(d->h_out, d->norm_gain, d->hn, d->T, d->d_model, d->eps, s, pdl)) return rc;
+      if (int rc = gate_up_bf16(&f, status, s, pdl)) return rc;
       // out = h_mid Wd + h (the pre-norm state), written in place over h
-      if (int rc = down_bf16(&f, status, s)) return rc;
+      if (int rc = down_bf16(&f, status, s, pdl)) return rc;
     }
     return BELL_OK;
   }

@@ -76,6 +76,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Programmatic dependent launch.  griddep_wait: block until the grid this
+// one depends on (the previous kernel in the stream, when this one was
+// launched with cudaLaunchAttributeProgrammaticStreamSerialization) has
+// completed and its writes are visible; a no-op otherwise.  griddep_launch:
+// this CTA no longer holds back that attribute's dependent launch (once every
+// CTA has called it or exited, the next kernel's CTAs may start and run up to
+// their own griddep_wait).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
