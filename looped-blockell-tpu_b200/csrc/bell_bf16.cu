@@ -612,7 +612,7 @@ int check_ffn(const BellFFNDesc* d, int dtype) {
   return BELL_OK;
 }
 
-int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl) {
+int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl, int64_t ld_h, int64_t h_parts) {
   const BellEll &g = d->gate, &u = d->up;
   const bool sm = g.B < 64;  // small tiles: bell_small.cu
   CUtensorMap ma, mg, mu;
@@ -638,7 +638,8 @@ int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl
   p.plan = reinterpret_cast<const uint32_t*>(static_cast<const char*>(d->plan) + L.gu_entries);
   p.counts = reinterpret_cast<const int32_t*>(static_cast<const char*>(d->plan) + L.gu_counts);
   p.out = d->h;
-  p.ld_out = d->d_ff;
+  p.ld_out = ld_h > 0 ? ld_h : d->d_ff;
+  p.h_parts = h_parts;
   p.gate_pre = d->gate_pre;
   p.up_out = d->up_out;
   p.status = status;

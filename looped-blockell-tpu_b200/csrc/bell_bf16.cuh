@@ -70,6 +70,10 @@ struct Bf16Params {
   // launch with programmatic stream serialization (the engine kernel waits for
   // its predecessor after its shared-memory / TMEM set-up; tile 64/128 engine only)
   int32_t pdl;
+  // gate/up of the fp32 path on the tensor cores (tile-64 engine only): with
+  // h_parts > 0 the epilogue writes the exact fp32 silu(g) * u as three bf16
+  // parts at out[t * ld_out + part * h_parts + f], part = 0, 1, 2
+  int64_t h_parts;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {

@@ -503,6 +503,30 @@ __device__ bool epilogue(const Bf16Params& p, const Smem& s, uint32_t tmem, int 
             if (!any1) v[t] = 0u;
           }
         }
+        if (p.h_parts) {  // fp32 path on the tensor cores: exact SiLU*up, stored as three bf16 parts
+          if (row_ok) {
+            __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out + int64_t(r) * B + j * 32;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              uint32_t w0[4], w1[4], w2[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int c0 = 8 * t + 2 * e;
+                float a0, b0, z0, a1, b1, z1;
+                split3_bf16(silu_mul_exact(__uint_as_float(g[c0]) * rs, __uint_as_float(v[c0]) * rs), a0, b0, z0);
+                split3_bf16(silu_mul_exact(__uint_as_float(g[c0 + 1]) * rs, __uint_as_float(v[c0 + 1]) * rs), a1, b1,
+                            z1);
+                w0[e] = pack_bf16x2(a0, a1);
+                w1[e] = pack_bf16x2(b0, b1);
+                w2[e] = pack_bf16x2(z0, z1);
+              }
+              st_global_v4(hrow + t * 8, w0[0], w0[1], w0[2], w0[3]);
+              st_global_v4(hrow + p.h_parts + t * 8, w1[0], w1[1], w1[2], w1[3]);
+              st_global_v4(hrow + 2 * p.h_parts + t * 8, w2[0], w2[1], w2[2], w2[3]);
+            }
+          }
+          continue;
+        }
         uint32_t hp[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {

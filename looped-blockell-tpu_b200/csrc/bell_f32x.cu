@@ -18,15 +18,19 @@
 // column base + x_part * part_cols + c.  The down projection gets three
 // more slots per block-row r: identity tiles on the x-region parts of column
 // block r, so the residual x0 + x1 + x2 is added inside the same fp32
-// accumulator.  The forward then runs on the bf16 Block-ELL linear kernels
-// (fp32 output): gate and up from A's x region, SiLU*up in fp32 and its split
-// into A's h region, down from A.  Semantics: looped_blockell/layers/
+// accumulator.  The forward then runs on the bf16 Block-ELL kernels: gate and
+// up from A's x region (at tile size 64 with enough work, one gate/up kernel
+// whose epilogue writes the exact fp32 SiLU*up as three bf16 parts into A's h
+// region; else two linears with fp32 output, then SiLU*up in fp32 split into
+// A), and the down linear (fp32 output) from A.  Semantics: looped_blockell/layers/
 // block_ell.py:149-182 and mlp.py:119-145 (the reference computes in fp32).
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <string>
 
 #include "bell_host.h"
+#include "bell_ptx.cuh"
 
 namespace bell {
 
@@ -37,11 +41,11 @@ __constant__ int8_t kXPart[6] = {0, 0, 1, 0, 1, 2};
 __constant__ int8_t kWPart[6] = {0, 1, 0, 2, 1, 0};
 
 __device__ __forceinline__ void split3(float v, __nv_bfloat16& a, __nv_bfloat16& b, __nv_bfloat16& c) {
-  a = __float2bfloat16_rn(v);
-  const float r1 = v - __bfloat162float(a);
-  b = __float2bfloat16_rn(r1);
-  const float r2 = r1 - __bfloat162float(b);
-  c = __float2bfloat16_rn(r2);
+  float p0, p1, p2;
+  split3_bf16(v, p0, p1, p2);
+  a = __float2bfloat16_rn(p0);
+  b = __float2bfloat16_rn(p1);
+  c = __float2bfloat16_rn(p2);
 }
 
 // One thread per element of one original tile: writes that element of its
@@ -105,8 +109,6 @@ __global__ void f32x_split_kernel(const float* __restrict__ src, int64_t T, int3
   }
 }
 
-__device__ __forceinline__ float silu_f32(float g) { return g / (1.f + expf(-g)); }
-
 // h = silu(g) * u in fp32 (optionally stored), split into dst[t, p F + j].
 __global__ void f32x_silu_split_kernel(const float* __restrict__ g, const float* __restrict__ u, int64_t T,
                                        int32_t F, float* __restrict__ h, __nv_bfloat16* __restrict__ dst,
@@ -118,8 +120,8 @@ __global__ void f32x_silu_split_kernel(const float* __restrict__ g, const float*
     const int32_t j = int32_t(i % n4) * 4;
     const float4 gv = *reinterpret_cast<const float4*>(g + t * F + j);
     const float4 uv = *reinterpret_cast<const float4*>(u + t * F + j);
-    const float4 hv = make_float4(silu_f32(gv.x) * uv.x, silu_f32(gv.y) * uv.y, silu_f32(gv.z) * uv.z,
-                                  silu_f32(gv.w) * uv.w);
+    const float4 hv = make_float4(silu_mul_exact(gv.x, uv.x), silu_mul_exact(gv.y, uv.y), silu_mul_exact(gv.z, uv.z),
+                                  silu_mul_exact(gv.w, uv.w));
     if (h) *reinterpret_cast<float4*>(h + t * F + j) = hv;
     __nv_bfloat16 a[4], b[4], c[4];
     split3(hv.x, a[0], b[0], c[0]);
@@ -143,6 +145,21 @@ int grid_for(int64_t n, int threads) {
 
 size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
+// The fused gate/up kernel (both projections in one unit, twice the steps of
+// a linear's unit) once there are at least kFusedUnitsPerSm units per SM;
+// with fewer the unit count leaves a tail.  Config 1's shapes on B200, fused
+// against two linears: T=1024 (1.7 units per SM) 0.109 / 0.096 ms, T=4096
+// 0.142 / 0.153 ms, T=8192 0.218 / 0.248 ms, T=65536 1.17 / 1.54 ms.
+// BELL_F32X_FUSED=0/1 forces one or the other.
+constexpr int64_t kFusedUnitsPerSm = 4;
+bool fused_gate_up(int64_t T, int32_t R_gu) {
+  const char* e = std::getenv("BELL_F32X_FUSED");
+  if (e && (e[0] == '0' || e[0] == '1')) return e[0] == '1';
+  int sms = 0;
+  if (device_sm_count(&sms) || sms < 1) sms = 148;
+  return ((T + 127) / 128) * int64_t(R_gu) >= kFusedUnitsPerSm * sms;
+}
+
 struct F32xWs {
   size_t a, g, u, plan, total;
 };
@@ -150,8 +167,12 @@ struct F32xWs {
 F32xWs f32x_ws(int64_t T, int32_t d_model, int32_t d_ff, int32_t B, int32_t K_g6, int32_t K_u6, int32_t K_d6) {
   F32xWs w{};
   const int32_t R_gu = d_ff / B, R_d = d_model / B;
-  size_t plan = plan_layout(0, 0, 0, R_gu, K_g6).total;
-  const size_t pu = plan_layout(0, 0, 0, R_gu, K_u6).total, pd = plan_layout(0, 0, 0, R_d, K_d6).total;
+  // one plan buffer, used in turn by each launch: the fused gate/up's plan
+  // (gate, up and down lists) or the gate / up / down linears' plans
+  size_t plan = plan_layout(R_gu, K_g6, K_u6, R_d, K_d6).total;
+  const size_t pg = plan_layout(0, 0, 0, R_gu, K_g6).total, pu = plan_layout(0, 0, 0, R_gu, K_u6).total,
+               pd = plan_layout(0, 0, 0, R_d, K_d6).total;
+  if (pg > plan) plan = pg;
   if (pu > plan) plan = pu;
   if (pd > plan) plan = pd;
   w.a = 0;
@@ -261,10 +282,32 @@ int bell_swiglu_fwd_f32x(const BellFFNDesc* d, void* workspace, void* stream) {
   const int64_t xcol = 3 * int64_t(F);  // first column of A's x region
   f32x_split_kernel<<<grid_for(T * (dm / 4), 256), 256, 0, s>>>(static_cast<const float*>(d->x), T, dm, A, LA, xcol);
   if (int rc = check_launch("f32x_split_kernel")) return rc;
-  if (int rc = linear(T, A, g, gb, d, s, plan)) return rc;
-  if (int rc = linear(T, A, u, ub, d, s, plan)) return rc;
-  f32x_silu_split_kernel<<<grid_for(T * (F / 4), 256), 256, 0, s>>>(gb, ub, T, F, static_cast<float*>(d->h), A, LA);
-  if (int rc = check_launch("f32x_silu_split_kernel")) return rc;
+  if (B == 64 && !d->h && !d->gate_pre && !d->up_out && fused_gate_up(T, g.R)) {
+    // tile 64 without fp32 intermediates: one gate/up kernel whose epilogue
+    // writes the exact fp32 silu(g) * u straight into A's h parts
+    int32_t* status = d->status ? d->status : default_status_ptr();
+    if (!status) return BELL_ERR_LAUNCH;
+    BellFFNDesc f{};
+    f.T = T;
+    f.d_model = int32_t(LA);  // the activation rows the gate/up kernel reads are A's
+    f.d_ff = F;
+    f.dtype = BELL_DTYPE_BF16;
+    f.x = A;
+    f.h = A;
+    f.plan = plan;
+    f.gate = g;
+    f.up = u;
+    f.down = w;
+    f.max_ctas = d->max_ctas;
+    if (int rc = launch_ffn_plan(&f, status, s)) return rc;
+    if (int rc = gate_up_bf16(&f, status, s, false, LA, F)) return rc;
+  } else {
+    if (int rc = linear(T, A, g, gb, d, s, plan)) return rc;
+    if (int rc = linear(T, A, u, ub, d, s, plan)) return rc;
+    f32x_silu_split_kernel<<<grid_for(T * (F / 4), 256), 256, 0, s>>>(gb, ub, T, F, static_cast<float*>(d->h), A,
+                                                                      LA);
+    if (int rc = check_launch("f32x_silu_split_kernel")) return rc;
+  }
   if (ident) {
     // the identity slots add whatever A's x region holds: x itself, the
     // caller's residual, or zeros when no residual is wanted

@@ -62,7 +62,10 @@ int check_ffn(const BellFFNDesc* d, int dtype);
 int launch_ffn_plan(const BellFFNDesc* d, int32_t* status, cudaStream_t s);
 // pdl: launch with programmatic stream serialization (honoured by the tile-64/
 // 128 token-major engine, which waits for its predecessor after its set-up).
-int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl = false);
+// ld_h > 0: row stride of h in elements (default d_ff); h_parts > 0: write
+// h as three bf16 parts of the exact fp32 value (tile 64 only, see Bf16Params).
+int gate_up_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl = false, int64_t ld_h = 0,
+                 int64_t h_parts = 0);
 int down_bf16(const BellFFNDesc* d, int32_t* status, cudaStream_t s, bool pdl = false);
 
 // Workspace of the loop: per-tile counters, per-row partial sums of squares

@@ -436,6 +436,22 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
+// fp32 SiLU*up of the fp32 path on the tensor cores: IEEE expf and divide,
+// each rounding explicit (no contraction), so every caller gets the same bits.
+__device__ __forceinline__ float silu_mul_exact(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+}
+
+// v = p0 + p1 + p2 (+ at most 2^-27 |v|): three bf16 parts, round to
+// nearest, each difference exact in fp32; returned as the fp32 values of the
+// bf16 parts (pack_bf16x2 of them is exact).
+__device__ __forceinline__ void split3_bf16(float v, float& p0, float& p1, float& p2) {
+  p0 = __bfloat162float(__float2bfloat16_rn(v));
+  const float r1 = __fsub_rn(v, p0);
+  p1 = __bfloat162float(__float2bfloat16_rn(r1));
+  p2 = __bfloat162float(__float2bfloat16_rn(__fsub_rn(r1, p1)));
+}
+
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");

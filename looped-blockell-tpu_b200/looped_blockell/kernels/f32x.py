@@ -13,8 +13,8 @@ methods reach its rel-L2 <= 1e-5 target:
 below that (smaller calls were not measured) or when an expanded row would
 exceed the forward's 254 slots.  Measured on B200 at config 1's shapes
 (d=512, F=2048, B=64, 25 %), SIMT against bf16x6: T=1024 0.214 / 0.096 ms,
-T=8192 0.721 / 0.256 ms, T=65536 5.34 / 1.54 ms, T=262144 22.5 / 6.25 ms
-(18 against 66 effective fp32 TFLOP/s).  ``BELL_F32_METHOD`` overrides the
+T=8192 0.721 / 0.218 ms, T=65536 5.34 / 1.17 ms, T=262144 22.5 / 4.84 ms
+(18 against 85 effective fp32 TFLOP/s).  ``BELL_F32_METHOD`` overrides the
 default.
 
 The expanded weights (bf16 tiles and column indices, 3x the fp32 bytes) are

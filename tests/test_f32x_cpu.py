@@ -48,7 +48,10 @@ def test_slots_and_workspace_bytes():
     assert lib.bell_f32x_slots(8, 0) == 48 and lib.bell_f32x_slots(8, 1) == 51
     T, d, F, B = 1000, 512, 2048, 64
     up = lambda v: (v + 255) // 256 * 256  # noqa: E731
-    plan = max(lib.bell_plan_bytes(0, 0, 0, F // B, 12), lib.bell_plan_bytes(0, 0, 0, d // B, 51))
+    # one plan buffer, used in turn: the fused gate/up's (gate, up and down
+    # lists) or each linear's
+    plan = max(lib.bell_plan_bytes(F // B, 12, 12, d // B, 51), lib.bell_plan_bytes(0, 0, 0, F // B, 12),
+               lib.bell_plan_bytes(0, 0, 0, d // B, 51))
     want = up(T * (3 * F + 3 * d) * 2) + 2 * up(T * F * 4) + up(plan)
     assert lib.bell_f32x_workspace_bytes(T, d, F, B, 12, 12, 51) == want
     assert lib.bell_f32x_workspace_bytes(-1, d, F, B, 12, 12, 51) == 0

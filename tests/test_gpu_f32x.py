@@ -1,12 +1,14 @@
 """The fp32 forward on the bf16 tensor cores (bf16x6 split) against the fp64
 oracle at the fp32 target, rel-L2 <= 1e-5, and against the CUDA-core fp32
 path.  Covers BASELINE config 1 at full size (both tile layouts, residual on
-and off, the intermediates), ragged and tiny token counts, tile sizes 32 and
+and off, the intermediates; the fused tile-64 gate/up kernel that writes
+h's bf16 parts itself and the two fp32-output linears), ragged and tiny token counts, tile sizes 32 and
 128, dead and duplicate slots, K_gate != K_up, a residual other than x, a
 weight updated in place between calls (the expanded weights are cached per
 tensor version), a 65536-token row sample, and the C ABI's argument checks."""
 
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -42,6 +44,17 @@ def test_config1_bf16x6_matches_oracle(layout):
         ro, rh, rg, ru = oracle_ffn(_f64(c), add_residual=add_res)
         for got, ref in ((out, ro), (h, rh), (g, rg), (u, ru)):
             assert O.rel_l2(got.cpu().numpy(), ref) < TOL_F32
+        # without intermediates, tile 64 runs one gate/up kernel that writes the
+        # bf16 parts of h itself (the call above ran two fp32-output linears)
+        for fused in ("0", "1"):
+            os.environ["BELL_F32X_FUSED"] = fused
+            try:
+                out2 = K.block_ell_swiglu_fwd(dc["x"], dc["vg"], dc["cg"], dc["vu"], dc["cu"], dc["vd"], dc["cd"],
+                                              add_residual=add_res, layout=layout, fp32_method="bf16x6")
+            finally:
+                del os.environ["BELL_F32X_FUSED"]
+            assert O.rel_l2(out2.cpu().numpy(), ro) < TOL_F32
+            assert O.rel_l2(out2.cpu().numpy(), out.cpu().numpy().astype(np.float64)) < 1e-6
         assert K.read_status() == 0
 
 
