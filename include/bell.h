@@ -205,6 +205,18 @@ size_t bell_f32x_workspace_bytes(int64_t T, int32_t d_model, int32_t d_ff, int32
                                  int32_t K_up6, int32_t K_down6);
 int bell_swiglu_fwd_f32x(const BellFFNDesc* desc, void* workspace, void* stream);
 
+/* One fp32 Block-ELL linear the same way (replaces the fp32 evaluation of
+ * block_ell_matmul, looped_blockell/layers/block_ell.py:149-182).  Activation
+ * matrix A = [x parts | residual parts] ([T, 3 in + 3 out] bf16; [T, 3 in]
+ * when the weight has no identity slots).  Expand the weight with
+ * col_base = 0, part_cols = C (= in/B) and, for a residual, ident_base = 3 C,
+ * ident_stride = R; desc->w is the expanded matrix (its C counts A's column
+ * blocks), dtype and out_dtype are F32, residual_row_lo/hi must be 0, plan is
+ * unused.  `workspace` holds bell_f32x_linear_workspace_bytes() bytes. */
+size_t bell_f32x_linear_workspace_bytes(int64_t T, int32_t in_features, int32_t out_features, int32_t R,
+                                        int32_t K6);
+int bell_linear_f32x(const BellLinearDesc* desc, void* workspace, void* stream);
+
 /* ---------------------------------------------------------------- ternary */
 
 /*

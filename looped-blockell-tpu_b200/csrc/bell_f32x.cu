@@ -321,4 +321,66 @@ int bell_swiglu_fwd_f32x(const BellFFNDesc* d, void* workspace, void* stream) {
   return linear(T, A, w, static_cast<float*>(d->out), d, s, plan);
 }
 
+// One fp32 Block-ELL linear, y = x W (+ residual), the same way: A = [x parts
+// | residual parts] ([T, 3 in_f + 3 out_f] bf16; [T, 3 in_f] without the
+// identity slots), w expanded with col_base = 0, part_cols = C and, for the
+// residual, ident_base = 3 C, ident_stride = R.
+size_t bell_f32x_linear_workspace_bytes(int64_t T, int32_t in_f, int32_t out_f, int32_t R, int32_t K6) {
+  if (T < 0 || in_f < 1 || out_f < 1 || R < 1 || K6 < 1) return 0;
+  const size_t la = 3 * size_t(in_f) + (K6 % 6 == 3 ? 3 * size_t(out_f) : 0);
+  return up256(size_t(T) * la * 2) + up256(plan_layout(0, 0, 0, R, K6).total);
+}
+
+int bell_linear_f32x(const BellLinearDesc* d, void* workspace, void* stream) {
+  if (!d) return fail(BELL_ERR_ARG, "descriptor is NULL");
+  if (d->dtype != BELL_DTYPE_F32 || d->out_dtype != BELL_DTYPE_F32)
+    return fail(BELL_ERR_DTYPE, "bell_linear_f32x: dtype and out_dtype must be BELL_DTYPE_F32");
+  const BellEll& w = d->w;
+  const int32_t B = w.B;
+  if (B != 16 && B != 32 && B != 64 && B != 128)
+    return fail(BELL_ERR_SHAPE, "bell_linear_f32x: tile size B must be 16, 32, 64 or 128");
+  const bool ident = w.K % 6 == 3;
+  if (w.R < 1 || w.K < 6 || (w.K % 6 != 0 && !ident))
+    return fail(BELL_ERR_SHAPE, "bell_linear_f32x: expanded rows hold 6K slots (6K + 3 with the residual's)");
+  const int32_t rest = w.C - (ident ? 3 * w.R : 0);  // 3 C column blocks of x parts
+  if (rest < 3 || rest % 3)
+    return fail(BELL_ERR_SHAPE, "bell_linear_f32x: the weight must be a bell_f32x_expand_ell output over [x parts"
+                                " | residual parts]");
+  if (d->add_residual && !ident)
+    return fail(BELL_ERR_ARG, "bell_linear_f32x: add_residual needs a weight expanded with identity slots");
+  if (d->residual_row_lo || d->residual_row_hi)
+    return fail(BELL_ERR_ARG, "bell_linear_f32x: residual row ranges are a bf16 feature");
+  if (d->T < 0) return fail(BELL_ERR_SHAPE, "T must be >= 0");
+  if (d->T > 0 && (!d->x || !d->out || !workspace || (d->add_residual && !d->residual)))
+    return fail(BELL_ERR_ARG, "x, out, workspace (and residual with add_residual) must be non-NULL");
+  if (!aligned16(d->x) || !aligned16(d->out) || !aligned16(workspace) || (d->residual && !aligned16(d->residual)))
+    return fail(BELL_ERR_ALIGN, "bell_linear_f32x: buffers must be 16-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  if (d->T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t T = d->T;
+  const int32_t in_f = rest / 3 * B, out_f = w.R * B;
+  const int64_t LA = int64_t(w.C) * B;
+  __nv_bfloat16* A = static_cast<__nv_bfloat16*>(workspace);
+  void* plan = static_cast<char*>(workspace) + up256(size_t(T) * size_t(LA) * 2);
+  f32x_split_kernel<<<grid_for(T * (in_f / 4), 256), 256, 0, s>>>(static_cast<const float*>(d->x), T, in_f, A, LA, 0);
+  if (int rc = check_launch("f32x_split_kernel")) return rc;
+  if (ident) {  // the identity slots add A's residual region: the residual, or zeros
+    const float* res = d->add_residual ? static_cast<const float*>(d->residual) : nullptr;
+    f32x_split_kernel<<<grid_for(T * (out_f / 4), 256), 256, 0, s>>>(res, T, out_f, A, LA, 3 * int64_t(in_f));
+    if (int rc = check_launch("f32x_split_kernel")) return rc;
+  }
+  BellLinearDesc L{};
+  L.T = T;
+  L.dtype = BELL_DTYPE_BF16;
+  L.out_dtype = BELL_DTYPE_F32;
+  L.max_ctas = d->max_ctas;
+  L.x = A;
+  L.out = d->out;
+  L.plan = plan;
+  L.w = w;
+  L.status = d->status;
+  return bell_linear_bf16(&L, s);
+}
+
 }  // extern "C"

@@ -64,6 +64,22 @@ def resolve(method: Optional[str], T: int, K_gate: int, K_up: int, K_down: int) 
     return "bf16x6" if fits and T >= AUTO_MIN_TOKENS else "simt"
 
 
+def resolve_linear(method: Optional[str], T: int, K: int, residual: bool) -> str:
+    """The method an fp32 linear of T tokens runs (6K slots per expanded row,
+    plus 3 identity slots for a residual)."""
+    m = method or default_method()
+    if m not in METHODS:
+        raise RuntimeError(f"fp32 method must be one of {METHODS}, got {m!r}")
+    fits = 6 * K + (3 if residual else 0) <= 254
+    if m == "bf16x6":
+        if not fits:
+            raise RuntimeError("bf16x6 needs at most 42 slots per row (41 with a residual)")
+        return m
+    if m == "simt":
+        return m
+    return "bf16x6" if fits and T >= AUTO_MIN_TOKENS else "simt"
+
+
 def _expand(values: torch.Tensor, cols: torch.Tensor, C_blocks: int, layout: int, col_base: int, part_cols: int,
             ident_base: int, ident_stride: int):
     key = (id(values), id(cols), C_blocks, layout, col_base, part_cols, ident_base, ident_stride)
@@ -90,6 +106,34 @@ def _expand(values: torch.Tensor, cols: torch.Tensor, C_blocks: int, layout: int
     while len(_CACHE) > _CACHE_MAX:
         _CACHE.popitem(last=False)
     return result
+
+
+def linear_f32x(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, residual: Optional[torch.Tensor],
+                layout: int, out: torch.Tensor) -> None:
+    """bell_linear_f32x on validated contiguous fp32 tensors: out = x W
+    (+ residual), x [T, C*B], tiles [R, K, B, B]."""
+    lib = _lib.load()
+    T, in_f = x.shape
+    R, K, B, _ = values.shape
+    Cx = in_f // B
+    ident = residual is not None
+    w6, c6 = _expand(values, cols, Cx, layout, 0, Cx, 3 * Cx if ident else -1, R if ident else 0)
+    CA = 3 * Cx + (3 * R if ident else 0)
+    ws = torch.empty(int(lib.bell_f32x_linear_workspace_bytes(T, in_f, R * B, R, w6.shape[1])), dtype=torch.uint8,
+                     device=x.device)
+    desc = _lib.BellLinearDesc()
+    desc.T = T
+    desc.dtype = desc.out_dtype = _lib.BELL_DTYPE_F32
+    desc.add_residual = 1 if ident else 0
+    desc.x, desc.out, desc.plan = x.data_ptr(), out.data_ptr(), None
+    desc.residual = residual.data_ptr() if ident else None
+    desc.w = _lib.BellEll(w6.data_ptr(), c6.data_ptr(), R, CA, w6.shape[1], B, layout, 0)
+    desc.status = None
+    desc.max_ctas = 0
+    stream = C.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    with torch.cuda.device(x.device):
+        _lib.check(lib.bell_linear_f32x(C.byref(desc), C.c_void_p(ws.data_ptr()), stream),
+                   "block_ell_linear (fp32, bf16x6)")
 
 
 def swiglu_fwd_f32x(x, vg, cg, vu, cu, vd, cd, add_residual: bool, layout: int, out: torch.Tensor,

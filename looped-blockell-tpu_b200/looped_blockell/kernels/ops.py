@@ -191,11 +191,13 @@ def block_ell_swiglu_fwd_with_intermediate(x, v_gate, ci_gate, v_up, ci_up, v_do
 def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, residual: Optional[torch.Tensor] = None,
                      out_dtype: Optional[torch.dtype] = None, layout: int = TILE_IN_OUT,
                      out: Optional[torch.Tensor] = None, residual_rows: Optional[Sequence[int]] = None,
-                     max_ctas: int = 0) -> torch.Tensor:
+                     max_ctas: int = 0, fp32_method: Optional[str] = None) -> torch.Tensor:
     """``y = x @ W^T (+ residual)`` for one Block-ELL weight; x is [N, C*B].
 
     bf16 only: ``residual_rows=(lo, hi)`` adds the residual to output rows
-    [lo, hi) only, and ``max_ctas`` caps the persistent grid (0 = every SM)."""
+    [lo, hi) only, and ``max_ctas`` caps the persistent grid (0 = every SM).
+    fp32 inputs run ``fp32_method`` (``kernels.f32x``): ``"auto"`` (default),
+    ``"simt"`` or ``"bf16x6"``."""
     lib = _lib.load()
     _check_cuda("x", x)
     if x.dim() != 2:
@@ -221,6 +223,10 @@ def block_ell_linear(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, 
         if residual.shape != (N, R * B) or residual.dtype != dtype:
             raise RuntimeError("residual must be [N, out_features] with the input dtype")
         residual = residual.contiguous()
+    if dtype == torch.float32 and residual_rows is None and max_ctas == 0 and \
+            f32x.resolve_linear(fp32_method, N, K, residual is not None) == "bf16x6":
+        f32x.linear_f32x(x, v, c, residual, layout, out)
+        return out
     plan = torch.empty(plan_bytes(0, 0, 0, R, K), dtype=torch.uint8, device=x.device)
     desc = _lib.BellLinearDesc()
     desc.T = N

@@ -1,11 +1,13 @@
 """The fp32 forward on the bf16 tensor cores (bf16x6 split) against the fp64
 oracle at the fp32 target, rel-L2 <= 1e-5, and against the CUDA-core fp32
 path.  Covers BASELINE config 1 at full size (both tile layouts, residual on
-and off, the intermediates; the fused tile-64 gate/up kernel that writes
-h's bf16 parts itself and the two fp32-output linears), ragged and tiny token counts, tile sizes 32 and
-128, dead and duplicate slots, K_gate != K_up, a residual other than x, a
-weight updated in place between calls (the expanded weights are cached per
-tensor version), a 65536-token row sample, and the C ABI's argument checks."""
+and off, the intermediates; the fused tile-64 gate/up kernel that writes h's
+bf16 parts itself and the two fp32-output linears), ragged and tiny token
+counts, tile sizes 32 and 128, dead and duplicate slots, K_gate != K_up, a
+residual other than x, a weight updated in place between calls (the expanded
+weights are cached per tensor version), a 65536-token row sample, the C ABI's
+argument checks, and the single fp32 linear (block_ell_matmul) the same way,
+alone and inside a trained BlockELLLinear."""
 
 import ctypes as C
 import os
@@ -158,3 +160,51 @@ def test_bf16x6_abi_rejects_bad_descriptors():
     assert lib.bell_f32x_expand_ell(C.byref(ell), 0, 2, -1, 0, C.c_void_p(v6.data_ptr()),
                                     C.c_void_p(c6.data_ptr()), None) == -2
     assert lib.bell_f32x_workspace_bytes(-1, 128, 512, 64, 12, 12, 27) == 0
+
+
+@pytest.mark.parametrize("B", [32, 64, 128])
+@pytest.mark.parametrize("layout", [O.LAYOUT_IN_OUT, O.LAYOUT_OUT_IN])
+def test_bf16x6_linear_matches_oracle(B, layout):
+    """One fp32 Block-ELL linear (block_ell_matmul) on the tensor cores, with
+    and without a residual, against the fp64 oracle and the CUDA-core path."""
+    from looped_blockell.kernels import block_ell_linear
+    rng = np.random.default_rng(B + layout)
+    T, C, R, K = 1000, 8, 6, 3
+    cols = np.stack([np.sort(rng.choice(C, K, replace=False)) for _ in range(R)]).astype(np.int32)
+    cols[2, 1] = -1  # a dead slot
+    vals = (rng.standard_normal((R, K, B, B)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((T, C * B)).astype(np.float32)
+    res = rng.standard_normal((T, R * B)).astype(np.float32)
+    dv = torch.from_numpy(vals if layout == O.LAYOUT_IN_OUT else np.swapaxes(vals, -1, -2).copy()).cuda()
+    dc, dx, dr = torch.from_numpy(cols).cuda(), torch.from_numpy(x).cuda(), torch.from_numpy(res).cuda()
+    ref = O.block_ell_matmul(x.astype(np.float64), vals.astype(np.float64), cols)
+    for residual in (None, dr):
+        want = ref if residual is None else ref + res.astype(np.float64)
+        got = block_ell_linear(dx, dv, dc, residual=residual, layout=layout, fp32_method="bf16x6")
+        simt = block_ell_linear(dx, dv, dc, residual=residual, layout=layout, fp32_method="simt")
+        assert O.rel_l2(got.cpu().numpy(), want) < TOL_F32
+        assert O.rel_l2(simt.cpu().numpy(), want) < TOL_F32
+
+
+def test_bf16x6_linear_layer_trains(monkeypatch):
+    """BlockELLLinear in fp32 with every linear (forward and the backward's
+    transposed products) on the bf16x6 path: output and gradients against the
+    dense float64 reference at the fp32 tolerance."""
+    from looped_blockell.layers import BlockELLLinear
+    from test_gpu_small_tiles import _dense_ref_linear
+    monkeypatch.setenv("BELL_F32_METHOD", "bf16x6")
+    B = 64
+    torch.manual_seed(3)
+    m = BlockELLLinear(8 * B, 4 * B, tile_size=B, density=0.5, dtype=torch.float32, device="cuda")
+    x = torch.randn(4, 300, 4 * B, device="cuda").requires_grad_(True)
+    y = m(x)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    cols = m.effective_col_indices().cpu().numpy()
+    vals = m.values.detach().double().cpu().numpy()
+    xf = x.detach().double().cpu().numpy().reshape(-1, 4 * B)
+    dyf = dy.double().cpu().numpy().reshape(-1, 8 * B)
+    ry, rdx, rdv = _dense_ref_linear(xf, vals, cols, B, 8 * B, 4 * B, dyf)
+    assert O.rel_l2(y.detach().double().cpu().numpy().reshape(-1, 8 * B), ry) < TOL_F32
+    assert O.rel_l2(x.grad.double().cpu().numpy().reshape(-1, 4 * B), rdx) < TOL_F32
+    assert O.rel_l2(m.values.grad.double().cpu().numpy(), rdv) < TOL_F32
