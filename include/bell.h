@@ -213,6 +213,14 @@ int bell_swiglu_fwd_f32x(const BellFFNDesc* desc, void* workspace, void* stream)
  * ident_stride = R; desc->w is the expanded matrix (its C counts A's column
  * blocks), dtype and out_dtype are F32, residual_row_lo/hi must be 0, plan is
  * unused.  `workspace` holds bell_f32x_linear_workspace_bytes() bytes. */
+/* Split fp32 rows into their three bf16 parts: src [T, n] (row stride
+ * ld_src) -> dst[t, col0 + p n + j], p = 0, 1, 2 (row stride ld_dst, bf16).
+ * The operand form of the fp32 tile gradients on the tensor cores (six
+ * bell_sddmm_bf16 calls over part slices, accumulated in fp32), which replace
+ * the fp32 evaluation of the reference's weight gradients
+ * (csrc/block_ell/swiglu_bwd.cu:13-14, 29-30). */
+int bell_f32x_split_rows(int64_t T, int32_t n, const float* src, int64_t ld_src, void* dst, int64_t ld_dst,
+                         int64_t col0, void* stream);
 size_t bell_f32x_linear_workspace_bytes(int64_t T, int32_t in_features, int32_t out_features, int32_t R,
                                         int32_t K6);
 int bell_linear_f32x(const BellLinearDesc* desc, void* workspace, void* stream);

@@ -86,9 +86,10 @@ __global__ void f32x_identity_kernel(int32_t R, int32_t K6, int32_t B, int32_t f
   }
 }
 
-// src [T, n] fp32 (NULL: zeros) -> parts at dst[t, col0 + p n + j] (row
-// stride ld_dst bf16 elements); four consecutive elements per thread.
-__global__ void f32x_split_kernel(const float* __restrict__ src, int64_t T, int32_t n,
+// src [T, n] fp32 (row stride ld_src; NULL: zeros) -> parts at
+// dst[t, col0 + p n + j] (row stride ld_dst bf16 elements); four consecutive
+// elements per thread.
+__global__ void f32x_split_kernel(const float* __restrict__ src, int64_t ld_src, int64_t T, int32_t n,
                                   __nv_bfloat16* __restrict__ dst, int64_t ld_dst, int64_t col0) {
   const int32_t n4 = n / 4;
   const int64_t total = T * n4;
@@ -96,7 +97,7 @@ __global__ void f32x_split_kernel(const float* __restrict__ src, int64_t T, int3
     const int64_t t = i / n4;
     const int32_t j = int32_t(i % n4) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (src) v = *reinterpret_cast<const float4*>(src + t * n + j);
+    if (src) v = *reinterpret_cast<const float4*>(src + t * ld_src + j);
     __nv_bfloat16 a[4], b[4], c[4];
     split3(v.x, a[0], b[0], c[0]);
     split3(v.y, a[1], b[1], c[1]);
@@ -280,7 +281,8 @@ int bell_swiglu_fwd_f32x(const BellFFNDesc* d, void* workspace, void* stream) {
   float* ub = d->up_out ? static_cast<float*>(d->up_out) : reinterpret_cast<float*>(ws + W.u);
   void* plan = ws + W.plan;
   const int64_t xcol = 3 * int64_t(F);  // first column of A's x region
-  f32x_split_kernel<<<grid_for(T * (dm / 4), 256), 256, 0, s>>>(static_cast<const float*>(d->x), T, dm, A, LA, xcol);
+  f32x_split_kernel<<<grid_for(T * (dm / 4), 256), 256, 0, s>>>(static_cast<const float*>(d->x), dm, T, dm, A, LA,
+                                                                 xcol);
   if (int rc = check_launch("f32x_split_kernel")) return rc;
   if (B == 64 && !d->h && !d->gate_pre && !d->up_out && fused_gate_up(T, g.R)) {
     // tile 64 without fp32 intermediates: one gate/up kernel whose epilogue
@@ -314,11 +316,28 @@ int bell_swiglu_fwd_f32x(const BellFFNDesc* d, void* workspace, void* stream) {
     const float* res = !d->add_residual ? nullptr : (d->residual ? static_cast<const float*>(d->residual)
                                                                   : static_cast<const float*>(d->x));
     if (res != d->x) {
-      f32x_split_kernel<<<grid_for(T * (dm / 4), 256), 256, 0, s>>>(res, T, dm, A, LA, xcol);
+      f32x_split_kernel<<<grid_for(T * (dm / 4), 256), 256, 0, s>>>(res, dm, T, dm, A, LA, xcol);
       if (int rc = check_launch("f32x_split_kernel")) return rc;
     }
   }
   return linear(T, A, w, static_cast<float*>(d->out), d, s, plan);
+}
+
+int bell_f32x_split_rows(int64_t T, int32_t n, const float* src, int64_t ld_src, void* dst, int64_t ld_dst,
+                         int64_t col0, void* stream) {
+  if (T < 0 || n < 4 || n % 4 || ld_src < n || ld_src % 4 || ld_dst < col0 + 3 * int64_t(n) || ld_dst % 4 ||
+      col0 < 0 || col0 % 4)
+    return fail(BELL_ERR_SHAPE, "bell_f32x_split_rows: need n, ld_src, ld_dst, col0 multiples of 4 with "
+                                "ld_src >= n and ld_dst >= col0 + 3 n");
+  if (T > 0 && (!src || !dst)) return fail(BELL_ERR_ARG, "bell_f32x_split_rows: NULL pointer");
+  if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7u))
+    return fail(BELL_ERR_ALIGN, "bell_f32x_split_rows: src must be 16-byte and dst 8-byte aligned");
+  if (int rc = require_sm100()) return rc;
+  if (T == 0) return BELL_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  f32x_split_kernel<<<grid_for(T * (n / 4), 256), 256, 0, s>>>(src, ld_src, T, n, static_cast<__nv_bfloat16*>(dst),
+                                                                ld_dst, col0);
+  return check_launch("f32x_split_kernel");
 }
 
 // One fp32 Block-ELL linear, y = x W (+ residual), the same way: A = [x parts
@@ -363,11 +382,12 @@ int bell_linear_f32x(const BellLinearDesc* d, void* workspace, void* stream) {
   const int64_t LA = int64_t(w.C) * B;
   __nv_bfloat16* A = static_cast<__nv_bfloat16*>(workspace);
   void* plan = static_cast<char*>(workspace) + up256(size_t(T) * size_t(LA) * 2);
-  f32x_split_kernel<<<grid_for(T * (in_f / 4), 256), 256, 0, s>>>(static_cast<const float*>(d->x), T, in_f, A, LA, 0);
+  f32x_split_kernel<<<grid_for(T * (in_f / 4), 256), 256, 0, s>>>(static_cast<const float*>(d->x), in_f, T, in_f, A,
+                                                                   LA, 0);
   if (int rc = check_launch("f32x_split_kernel")) return rc;
   if (ident) {  // the identity slots add A's residual region: the residual, or zeros
     const float* res = d->add_residual ? static_cast<const float*>(d->residual) : nullptr;
-    f32x_split_kernel<<<grid_for(T * (out_f / 4), 256), 256, 0, s>>>(res, T, out_f, A, LA, 3 * int64_t(in_f));
+    f32x_split_kernel<<<grid_for(T * (out_f / 4), 256), 256, 0, s>>>(res, out_f, T, out_f, A, LA, 3 * int64_t(in_f));
     if (int rc = check_launch("f32x_split_kernel")) return rc;
   }
   BellLinearDesc L{};

@@ -113,6 +113,8 @@ SIGNATURES = {
     "bell_f32x_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                                C.c_int32]),
     "bell_swiglu_fwd_f32x": (C.c_int, [C.POINTER(BellFFNDesc), C.c_void_p, C.c_void_p]),
+    "bell_f32x_split_rows": (C.c_int, [C.c_int64, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                       C.c_int64, C.c_void_p]),
     "bell_f32x_linear_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     "bell_linear_f32x": (C.c_int, [C.POINTER(BellLinearDesc), C.c_void_p, C.c_void_p]),
     "bell_swiglu_fwd_ternary": (C.c_int, [C.POINTER(BellTernaryFFNDesc), C.c_void_p]),

@@ -202,7 +202,9 @@ def block_ell_sddmm(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int
     """Tile gradients ``grad[r, k] (+)= a[:, c*B:(c+1)*B]^T b[:, r*B:(r+1)*B]``
     (c = cols[r, k]) in fp32, in ``layout``.  ``a``: [T, C*B], ``b``: [T, R*B]
     bf16 (tcgen05 at B = 64, 128; CUDA cores at 16, 32) or fp32 (CUDA cores,
-    ``bell_sddmm_f32``); either may be a column slice of a wider row-major
+    ``bell_sddmm_f32``, or at B = 64 / 128 six tcgen05 products of the
+    operands' bf16 parts, ``kernels.f32x``, as ``BELL_F32_METHOD`` and the
+    token count choose); either may be a column slice of a wider row-major
     tensor.  When ``out_bf16`` is given (bf16 operands only) it receives a
     bf16 copy.  Returns ``grad``."""
     for name, t in (("a", a), ("b", b), ("col_indices", cols)):
@@ -229,6 +231,10 @@ def block_ell_sddmm(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int
         accumulate = False
     elif grad.shape != (R, K, B, B) or grad.dtype != torch.float32 or not grad.is_contiguous():
         raise RuntimeError("grad must be a contiguous fp32 [R, K, B, B] tensor")
+    if f32 and T > 0:
+        from . import f32x  # fp32 on the tensor cores: six bf16 products of the operands' parts
+        if f32x.resolve_sddmm(None, T, B) == "bf16x6":
+            return f32x.sddmm_f32x(a, b, cols, B, layout, grad, accumulate)
     d = _lib.BellSddmmDesc()
     d.T = T
     d.a, d.b = a.data_ptr(), b.data_ptr()

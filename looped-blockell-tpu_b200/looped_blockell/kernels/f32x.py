@@ -136,6 +136,50 @@ def linear_f32x(x: torch.Tensor, values: torch.Tensor, cols: torch.Tensor, resid
                    "block_ell_linear (fp32, bf16x6)")
 
 
+# the six (a part, b part) products of a split product, leading terms first
+PAIRS = ((0, 0), (0, 1), (1, 0), (0, 2), (1, 1), (2, 0))
+
+
+def split_rows(src: torch.Tensor) -> torch.Tensor:
+    """[T, n] fp32 (rows may be strided, unit stride along n) -> [T, 3n] bf16
+    holding its three bf16 parts side by side (``bell_f32x_split_rows``)."""
+    T, n = src.shape
+    dst = torch.empty((T, 3 * n), dtype=torch.bfloat16, device=src.device)
+    stream = C.c_void_p(torch.cuda.current_stream(src.device).cuda_stream)
+    with torch.cuda.device(src.device):
+        _lib.check(_lib.load().bell_f32x_split_rows(T, n, C.c_void_p(src.data_ptr()), max(src.stride(0), n),
+                                                    C.c_void_p(dst.data_ptr()), 3 * n, 0, stream),
+                   "bell_f32x_split_rows")
+    return dst
+
+
+def resolve_sddmm(method: Optional[str], T: int, B: int) -> str:
+    """The method fp32 tile gradients of T tokens run: bf16x6 needs the
+    tcgen05 tile-gradient kernel (tile size 64 or 128)."""
+    m = method or default_method()
+    if m not in METHODS:
+        raise RuntimeError(f"fp32 method must be one of {METHODS}, got {m!r}")
+    if m == "simt" or B < 64:
+        return "simt"
+    if m == "bf16x6":
+        return m
+    return "bf16x6" if T >= AUTO_MIN_TOKENS else "simt"
+
+
+def sddmm_f32x(a: torch.Tensor, b: torch.Tensor, cols: torch.Tensor, B: int, layout: int, grad: torch.Tensor,
+               accumulate: bool) -> torch.Tensor:
+    """fp32 tile gradients grad[r, k] (+)= a[:, c*B:(c+1)*B]^T b[:, r*B:(r+1)*B]
+    as six bf16 tile-gradient products of the operands' parts, summed into
+    the fp32 ``grad``."""
+    from .backward import block_ell_sddmm
+    na, nb = a.shape[1], b.shape[1]
+    ap, bp = split_rows(a), split_rows(b)
+    for idx, (i, j) in enumerate(PAIRS):
+        block_ell_sddmm(ap[:, i * na:(i + 1) * na], bp[:, j * nb:(j + 1) * nb], cols, B, layout, grad=grad,
+                        accumulate=accumulate or idx > 0)
+    return grad
+
+
 def swiglu_fwd_f32x(x, vg, cg, vu, cu, vd, cd, add_residual: bool, layout: int, out: torch.Tensor,
                     h: Optional[torch.Tensor], gate_pre: Optional[torch.Tensor], up_out: Optional[torch.Tensor],
                     residual: Optional[torch.Tensor] = None) -> None:

@@ -6,8 +6,9 @@ bf16 parts itself and the two fp32-output linears), ragged and tiny token
 counts, tile sizes 32 and 128, dead and duplicate slots, K_gate != K_up, a
 residual other than x, a weight updated in place between calls (the expanded
 weights are cached per tensor version), a 65536-token row sample, the C ABI's
-argument checks, and the single fp32 linear (block_ell_matmul) the same way,
-alone and inside a trained BlockELLLinear."""
+argument checks, the single fp32 linear (block_ell_matmul) the same way,
+alone and inside a trained BlockELLLinear, and the fp32 tile gradients as six
+bf16 tile-gradient products."""
 
 import ctypes as C
 import os
@@ -208,3 +209,39 @@ def test_bf16x6_linear_layer_trains(monkeypatch):
     assert O.rel_l2(y.detach().double().cpu().numpy().reshape(-1, 8 * B), ry) < TOL_F32
     assert O.rel_l2(x.grad.double().cpu().numpy().reshape(-1, 4 * B), rdx) < TOL_F32
     assert O.rel_l2(m.values.grad.double().cpu().numpy(), rdv) < TOL_F32
+
+
+@pytest.mark.parametrize("B,layout,T", [(64, O.LAYOUT_IN_OUT, 3001), (128, O.LAYOUT_OUT_IN, 2048)])
+def test_bf16x6_tile_gradients_match_fp64(B, layout, T, monkeypatch):
+    """fp32 tile gradients as six tcgen05 products of the operands' bf16
+    parts (what ``auto`` picks from 1024 tokens up at tile 64/128): against
+    float64 sums, with a strided operand, a dead slot and accumulation onto
+    an existing gradient; and against the CUDA-core kernel."""
+    from looped_blockell.kernels import block_ell_sddmm, f32x
+    assert f32x.resolve_sddmm(None, T, B) == "bf16x6"
+    rng = np.random.default_rng(B + T)
+    R, Cc, Kk = 5, 4, 3
+    cols = np.stack([rng.choice(Cc, size=Kk, replace=False) for _ in range(R)]).astype(np.int32)
+    cols[2, 1] = -1
+    a = rng.standard_normal((T, Cc * B)).astype(np.float32)
+    bw = rng.standard_normal((T, 2 * R * B)).astype(np.float32)  # b is the right half of a wider row
+    base = rng.standard_normal((R, Kk, B, B)).astype(np.float32)
+    da, dbw, dcols = torch.from_numpy(a).cuda(), torch.from_numpy(bw).cuda(), torch.from_numpy(cols).cuda()
+    db = dbw[:, R * B:]
+    grad = torch.from_numpy(base).cuda()
+    block_ell_sddmm(da, db, dcols, B, layout, grad=grad, accumulate=True)
+    monkeypatch.setenv("BELL_F32_METHOD", "simt")
+    simt = block_ell_sddmm(da, db, dcols, B, layout)
+    b = bw[:, R * B:].astype(np.float64)
+    want = base.astype(np.float64).copy()
+    exact = np.zeros((R, Kk, B, B))
+    for r in range(R):
+        for k in range(Kk):
+            c = cols[r, k]
+            if c >= 0:
+                t = a[:, c * B:(c + 1) * B].astype(np.float64).T @ b[:, r * B:(r + 1) * B]
+                exact[r, k] = t if layout == O.LAYOUT_IN_OUT else t.T
+    want += exact
+    assert O.rel_l2(grad.cpu().numpy().astype(np.float64), want) < TOL_F32
+    assert O.rel_l2(simt.cpu().numpy().astype(np.float64), exact) < TOL_F32
+    assert np.all(simt.cpu().numpy()[cols < 0] == 0)
