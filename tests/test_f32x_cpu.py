@@ -56,3 +56,40 @@ def test_slots_and_workspace_bytes():
     assert lib.bell_f32x_workspace_bytes(T, d, F, B, 12, 12, 51) == want
     assert lib.bell_f32x_workspace_bytes(-1, d, F, B, 12, 12, 51) == 0
     assert lib.bell_f32x_workspace_bytes(T, d, F, B, 0, 12, 51) == 0
+
+
+def test_bad_arguments_rejected_before_any_launch():
+    """The fp32 tensor-core entry points check their descriptors on the host
+    first (no GPU needed): wrong dtypes, weights that are not expansions,
+    residual row ranges, split strides."""
+    import ctypes as C
+    from looped_blockell.kernels import _lib as L
+    lib = _lib()
+    d = L.BellFFNDesc()
+    d.T, d.d_model, d.d_ff, d.dtype = 16, 256, 512, L.BELL_DTYPE_BF16
+    d.x = d.out = 1024  # never dereferenced: validation fails first
+    assert lib.bell_swiglu_fwd_f32x(C.byref(d), C.c_void_p(1024), None) == -1
+    d.dtype = L.BELL_DTYPE_F32
+    CA = 3 * 8 + 3 * 4  # [h parts | x parts] at B = 64
+    d.gate = L.BellEll(1024, 1024, 8, CA, 12, 64, 0, 0)
+    d.up = L.BellEll(1024, 1024, 8, CA, 12, 64, 0, 0)
+    d.down = L.BellEll(1024, 1024, 4, CA, 26, 64, 0, 0)  # 26 = 6K + 2: not an expansion
+    assert lib.bell_swiglu_fwd_f32x(C.byref(d), C.c_void_p(1024), None) == -2
+    d.down = L.BellEll(1024, 1024, 4, CA, 24, 64, 0, 0)  # no identity slots ...
+    d.add_residual = 1  # ... but a residual asked for
+    assert lib.bell_swiglu_fwd_f32x(C.byref(d), C.c_void_p(1024), None) == -8
+    lin = L.BellLinearDesc()
+    lin.T, lin.dtype, lin.out_dtype = 16, L.BELL_DTYPE_F32, L.BELL_DTYPE_BF16
+    lin.x = lin.out = 1024
+    lin.w = L.BellEll(1024, 1024, 4, 3 * 4 + 3 * 4, 15, 64, 0, 0)
+    assert lib.bell_linear_f32x(C.byref(lin), C.c_void_p(1024), None) == -1
+    lin.out_dtype = L.BELL_DTYPE_F32
+    lin.residual_row_hi = 8
+    assert lib.bell_linear_f32x(C.byref(lin), C.c_void_p(1024), None) == -8
+    lin.residual_row_hi = 0
+    lin.w = L.BellEll(1024, 1024, 4, 3 * 4 + 3 * 4, 14, 64, 0, 0)  # 14 slots: not 6K or 6K + 3
+    assert lib.bell_linear_f32x(C.byref(lin), C.c_void_p(1024), None) == -2
+    # split: n and the strides must be multiples of 4, the parts must fit the row
+    assert lib.bell_f32x_split_rows(8, 6, C.c_void_p(1024), 8, C.c_void_p(1024), 64, 0, None) == -2
+    assert lib.bell_f32x_split_rows(8, 8, C.c_void_p(1024), 8, C.c_void_p(1024), 16, 0, None) == -2
+    assert lib.bell_f32x_linear_workspace_bytes(-1, 256, 256, 4, 15) == 0
