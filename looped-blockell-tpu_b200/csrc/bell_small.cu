@@ -17,10 +17,12 @@
 // K = 16 into the block-row's columns of the unit's accumulator, fp32 in
 // TMEM, double buffered (2 x 128 columns).
 //
-// Warps: 0 and 6 TMA producers (alternate stages; each walks the unit's plan
-// steps from a two-unit-deep register prefetch), 1 TMEM owner + MMA issuer,
-// 2-5 epilogue (one TMEM lane quadrant each, one token row per thread):
-// SiLU(gate) * up, or + residual, with 16-byte stores.
+// Warps: 0, 6, 7 and 8 TMA producers (every fourth stage each; each walks the
+// unit's plan steps from a two-unit-deep register prefetch), 1 TMEM owner +
+// MMA issuer, 2-5 epilogue (one TMEM lane quadrant each, one token row per
+// thread): SiLU(gate) * up, or + residual, with 16-byte stores.  A TMA copy
+// costs its issuing thread ~225 cycles whatever its size and a step here is
+// two or three small copies, so the copies are spread over four warps.
 #include <string>
 
 #include "bell_bf16.cuh"
@@ -31,8 +33,9 @@ namespace bell {
 namespace small {
 
 static constexpr int kM = 128;        // tokens per unit (MMA M)
-static constexpr int kThr = 7 * 32;   // warps 0-6
-static constexpr int kProd1 = 6;      // second producer warp
+static constexpr int kThr = 9 * 32;   // warps 0-8
+static constexpr int kProds = 4;      // TMA producer warps: 0, 6, 7, 8
+static constexpr int kProd1 = 6;      // first of the extra producer warps
 static constexpr int kAcc = 128;      // accumulator columns per buffer
 
 template <int B, bool GU>
@@ -46,6 +49,9 @@ struct SCfg {
   static constexpr int CTL = 1024;
   static constexpr int SMEM = NS * STAGE + 1024 + CTL;
   static_assert(G >= 1 && G <= 8, "rows per unit");
+  // producer p takes the steps g with g % kProds == p, so it always uses the
+  // same NS / kProds stages and waits on each one use behind (no parity aliasing)
+  static_assert(NS % kProds == 0, "stages per producer");
 };
 
 // stage-info word: [0,8) row of the group, then flags
@@ -157,9 +163,9 @@ __global__ void __launch_bounds__(kThr, 1)
   const int n_groups = (p.R + G - 1) / G;
   const int n_units = p.n_mtiles * n_groups;
 
-  if (warp == 0 || warp == kProd1) {
+  if (warp == 0 || warp >= kProd1) {
     // ---------------------------------------------------------- producers
-    const int pid = warp == 0 ? 0 : 1;
+    const int pid = warp == 0 ? 0 : warp - kProd1 + 1;
     if (pid == 0 && lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_w0);
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(kThr, 1)
         if (f > 0 && (f & 31) == 0) chunk = load_steps<G>(p, r0, cnt_this, f);  // long units: next 32 steps
         const uint32_t e = __shfl_sync(0xffffffffu, chunk.entry, f & 31);
         const int j = __shfl_sync(0xffffffffu, chunk.row, f & 31);
-        if (int(g & 1u) == pid) {
+        if (int(g % uint32_t(kProds)) == pid) {
           if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1, ctl))) {
             alive = false;
             break;
