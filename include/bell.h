@@ -26,7 +26,9 @@
  * [B_out, B_in], the reference CUDA kernels' convention
  * (csrc/block_ell/swiglu_fwd.cu:273-284).  A column index of -1 marks a dead
  * slot (looped_blockell/opt/column_reorder.py:131-136) that contributes
- * nothing.  B is 64 or 128.
+ * nothing.  B is 16, 32, 64 or 128 for the bf16 and fp32 entry points; the
+ * ternary path, the persistent loop kernel and bell_down_silu_bwd_bf16 name
+ * their own tile sizes below.
  */
 #ifndef BELL_H_
 #define BELL_H_
@@ -233,7 +235,7 @@ int bell_linear_f32x(const BellLinearDesc* desc, void* workspace, void* stream);
  * ([B_out][B_in]); each little-endian uint32 holds 16 consecutive B_in
  * entries of one output column, entry i at bits 2*(i%16); codes 00 = 0,
  * 01 = +1, 11 = -1.  scales: [R, K] fp32 (per-tile AbsMean,
- * bonsai-test/bitlinear.py:34-55 with group = one tile).
+ * bonsai-test/bitlinear.py:34-55 with group = one tile).  Tile size B = 64.
  */
 typedef struct BellTernaryEll {
   const uint8_t* packed;
@@ -376,7 +378,8 @@ int bell_silu_mul_bwd_bf16(int64_t T, int32_t d_ff, const void* d_h, const void*
  * down weight (R = d_ff / B block-rows over C = d_model / B column blocks).
  * grad_out: [T, d_model]; gate_pre, up_out: [T, d_ff]; d_gate_up: [T, 2 d_ff]
  * with d_gate in columns [0, d_ff) and d_up in [d_ff, 2 d_ff); all bf16.
- * plan: bell_plan_bytes(0, 0, 0, w_t.R, w_t.K) bytes.
+ * plan: bell_plan_bytes(0, 0, 0, w_t.R, w_t.K) bytes.  Tile size 64 or 128
+ * (smaller tiles: bell_linear_bf16, then bell_silu_mul_bwd_bf16).
  */
 typedef struct BellDownBwdDesc {
   int64_t T;
